@@ -1,0 +1,158 @@
+/*
+ * pf_b200.h -- C ABI of the sm_100a backend for PTXForge's one hot path:
+ *
+ *     C[r,c] = gelu_tanh( scale_a*scale_b * sum_k A[r,k]*B[k,c] + bias[c] )
+ *
+ * with A row-major [M x K], B row-major [K x N], bias fp32 [N], C row-major [M x N].
+ *
+ * This library replaces, for PTXForge's `Runner` boundary
+ * (core/include/ptxforge/runner.hpp:39-45), what `CudaRunner` does per trial
+ * (core/src/cuda_runner.cpp:152-217): select and load a kernel for a tile config,
+ * launch it, time it with the reference protocol and report kernel attributes.
+ * The reference's kernel ABI (kernels/gemm_bias_gelu.cu:42-44) is kept by the fp32 path:
+ * same operand order, same row-major layout, same GELU (tanh form, k0=0.7978845608028654,
+ * k1=0.044715, kernels/gemm_bias_gelu.cu:37-40).
+ *
+ * Conventions
+ *   - Every function returns PF_OK (0) on success or a nonzero PF_E* code.  Nothing here throws,
+ *     aborts or exits; the text of the last failure is available from pf_last_error().
+ *   - A pf_ctx belongs to one host thread and one GPU.  It is not thread-safe; use one context per
+ *     (thread, device), as the multi-GPU row-sharded runner does.
+ *   - Device pointers passed to pf_bind are owned by the caller.  Buffers used by pf_run_host are
+ *     owned by the context and freed by pf_close.
+ *   - Kernel-side waits are bounded: a wait that runs out sets a bit in the context's device status
+ *     word (read it with pf_device_status) and the kernel returns instead of hanging.
+ */
+#ifndef PF_B200_H
+#define PF_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+enum {
+  PF_OK = 0,
+  PF_EINVAL = 1,       /* bad argument (null pointer, non-positive size, ...)                   */
+  PF_ENODEV = 2,       /* no such CUDA device, or not an sm_100 part                            */
+  PF_ECUDA = 3,        /* a CUDA runtime / driver call failed                                   */
+  PF_ETILE = 4,        /* the tile config does not map onto a kernel of this backend            */
+  PF_ESHAPE = 5,       /* M/N/K violate a layout rule of the chosen path (e.g. TMA 16-B rows)   */
+  PF_ESTATE = 6,       /* call out of order (launch before prepare/bind, ...)                   */
+  PF_ETIMEOUT = 7,     /* a bounded device-side wait ran out; see pf_device_status              */
+  PF_ENOMEM = 8        /* device or pinned-host allocation failed                               */
+};
+
+/* ---- data types --------------------------------------------------------------------------- */
+typedef enum {
+  PF_F32 = 0,          /* fp32 A/B/C, fp32 FFMA (SIMT) accumulate, tanhf epilogue               */
+  PF_F32_3XTF32 = 1,   /* reserved: fp32 via three tf32 tensor-core products (not built yet)    */
+  PF_BF16 = 2,         /* bf16 A/B, fp32 accumulate in TMEM, bf16 C                             */
+  PF_E4M3 = 3          /* fp8 e4m3 A/B with per-tensor fp32 scales, fp32 accumulate, bf16 C     */
+} pf_dtype;
+
+/* The tuner's tile config: exactly the fields of ptxforge::Config (core/include/ptxforge/space.hpp:58).
+ *   fp32 path   : the reference meaning (block tile BM x BN, K step BK, TM x TN per thread, PAD).
+ *   tensor path : BM = CTA rows (128), BN = UMMA N (64/128/256), BK = K-block in 4-byte words
+ *                 (32 = one 128-byte swizzle row), TM = smem pipeline stages, TN = epilogue column
+ *                 chunks per TMEM load group, PAD = tile-raster group height in M blocks (0 = 16). */
+typedef struct {
+  int BM, BN, BK, TM, TN, PAD;
+} pf_tile;
+
+/* Opaque per-(thread, GPU) state: device, stream, selected kernel, tensor maps, status word. */
+typedef struct pf_ctx pf_ctx;
+
+/* Kernel attributes of the prepared variant (what CudaRunner reads with cuFuncGetAttribute and
+ * cuOccupancyMaxActiveBlocksPerMultiprocessor, core/src/cuda_runner.cpp:163-179). */
+typedef struct {
+  int regs;            /* registers per thread                                                   */
+  int local_bytes;     /* local (spill) bytes per thread                                        */
+  int smem_bytes;      /* static + dynamic shared memory per block                              */
+  int blocks_per_sm;   /* occupancy: resident blocks per SM                                     */
+  int threads;         /* threads per block                                                     */
+  int grid;            /* blocks launched (persistent kernels: min(tiles, SMs))                 */
+  int num_sms;         /* SMs on the device                                                     */
+} pf_attr;
+
+/* ---- lifecycle ---------------------------------------------------------------------------- */
+
+/* Open device `device` (CUDA ordinal).  Replaces CudaRunner::Impl's constructor
+ * (core/src/cuda_runner.cpp:65-79: cuInit, device, primary context). */
+int pf_open(int device, pf_ctx **out);
+
+/* Release everything the context owns.  Replaces CudaRunner::Impl::~Impl (cuda_runner.cpp:81-88). */
+int pf_close(pf_ctx *ctx);
+
+/* Select the kernel variant for (dtype, tile, M, N, K) and build its TMA tensor maps once the
+ * operands are bound.  Rejects configs this backend cannot run with PF_ETILE / PF_ESHAPE (an
+ * invalid config is a failed trial, never a crash: cuda_runner.cpp:171-175).  Replaces the
+ * per-trial compile + module load (cuda_runner.cpp:159-161, 219-237). */
+int pf_prepare(pf_ctx *ctx, pf_dtype dtype, const pf_tile *tile, int M, int N, int K);
+
+/* Bind caller-owned device operands (row-major).  A/B are float, bf16 or e4m3 bytes according to
+ * the prepared dtype; C is float for PF_F32 and bf16 otherwise.  scale_a/scale_b are the
+ * per-tensor dequantisation scales (used by PF_E4M3, must be 1 otherwise).  Replaces the
+ * parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} of cuda_runner.cpp:182. */
+int pf_bind(pf_ctx *ctx, const void *A, const void *B, const float *bias, void *C, float scale_a,
+            float scale_b);
+
+/* Launch once on `stream` (a cudaStream_t; NULL = the context's own stream).  Asynchronous.
+ * Replaces the cuLaunchKernel of cuda_runner.cpp:183. */
+int pf_launch(pf_ctx *ctx, void *stream);
+
+/* Reference timing protocol (CudaRunner::Impl::median_ms, cuda_runner.cpp:110-130): `warmup`
+ * launches, then `reps` repetitions of `iters` back-to-back launches between two events on the
+ * context's stream; per-launch time = elapsed/iters; returns the median over reps in ms. */
+int pf_time(pf_ctx *ctx, int warmup, int iters, int reps, double *median_ms);
+
+/* Kernel attributes of the prepared variant. */
+int pf_attrs(pf_ctx *ctx, pf_attr *out);
+
+/* Synchronise the context's stream and read (then clear) the device status word: 0 = clean,
+ * nonzero = a bounded device-side wait ran out (bit 0: TMA-producer wait, bit 1: MMA wait,
+ * bit 2: epilogue wait, bit 3: teardown wait). */
+int pf_device_status(pf_ctx *ctx, unsigned *err_word);
+
+/* Bound, in nanoseconds, on every device-side wait of subsequent launches (default 4e9). */
+int pf_set_wait_timeout(pf_ctx *ctx, unsigned long long ns);
+
+/* Text of the most recent failure on this context ("" if none).  Valid until the next call. */
+const char *pf_last_error(const pf_ctx *ctx);
+
+/* ---- host-buffer path (the end-to-end call a host-side caller makes) ---------------------- */
+
+/* Copy host operands in (pinned or pageable), launch the prepared kernel, copy C back, and
+ * synchronise.  Device buffers are owned by the context and re-used while the problem size is
+ * unchanged.  This is the one-call form of CudaRunner::Impl::ensure + launch + cuMemcpyDtoH
+ * (cuda_runner.cpp:91-108, 183-188). */
+int pf_run_host(pf_ctx *ctx, const void *hA, const void *hB, const float *hbias, void *hC,
+                float scale_a, float scale_b);
+
+/* ---- row sharding (no collective on the hot path) ----------------------------------------- */
+
+/* Rows [*row0, *row0 + *rows) of A and C that shard `g` of `G` owns for an M-row problem.  Shard
+ * boundaries are multiples of `align` rows (the CTA tile height) except for the last shard. */
+int pf_shard_rows(int M, int G, int g, int align, int *row0, int *rows);
+
+/* ---- utilities ---------------------------------------------------------------------------- */
+
+/* Bytes of one element of A/B and of C for a dtype (0 for an unknown dtype). */
+size_t pf_elem_bytes(pf_dtype dtype);
+size_t pf_out_bytes(pf_dtype dtype);
+
+/* Library version string, and the architecture the kernels were compiled for ("sm_100a"). */
+const char *pf_version(void);
+
+/* Self-test of the bounded wait: launches one block that waits on an mbarrier nothing arrives at,
+ * with a bound of `timeout_ns`.  Returns PF_OK and sets *err_word to the bit the kernel recorded
+ * (expected nonzero) -- the kernel returns on its own, the context stays usable. */
+int pf_selftest_wait_timeout(pf_ctx *ctx, unsigned long long timeout_ns, unsigned *err_word);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PF_B200_H */

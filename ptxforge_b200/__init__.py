@@ -1,0 +1,262 @@
+"""ptxforge_b200 -- sm_100a backend for PTXForge's fused GEMM + bias + GELU hot path.
+
+Python view of the C ABI in include/pf_b200.h (libpf_b200.so, built by ``ptxforge_b200.build``).
+It mirrors what PTXForge's CudaRunner does per trial (core/src/cuda_runner.cpp:152-217): pick a
+kernel for a tile config, bind operands, launch, time with the reference protocol, read kernel
+attributes.  There is no CPU fallback: without the library or an sm_100 GPU every call raises.
+
+    import torch, ptxforge_b200 as pf
+    C = pf.gemm_bias_gelu(A, B, bias, dtype="bf16")          # A, B, bias CUDA tensors
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from dataclasses import dataclass
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpf_b200.so")
+
+PF_OK, PF_EINVAL, PF_ENODEV, PF_ECUDA, PF_ETILE, PF_ESHAPE, PF_ESTATE, PF_ETIMEOUT, PF_ENOMEM = range(9)
+ERROR_NAMES = {0: "PF_OK", 1: "PF_EINVAL", 2: "PF_ENODEV", 3: "PF_ECUDA", 4: "PF_ETILE", 5: "PF_ESHAPE",
+               6: "PF_ESTATE", 7: "PF_ETIMEOUT", 8: "PF_ENOMEM"}
+
+DTYPES = {"f32": 0, "f32_3xtf32": 1, "bf16": 2, "e4m3": 3}
+ELEM_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 1}
+OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
+
+# Exported symbols (every entry point of include/pf_b200.h).
+SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
+           "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
+           "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout")
+
+
+class Tile(ctypes.Structure):
+    """ptxforge::Config (core/include/ptxforge/space.hpp:58): BM, BN, BK, TM, TN, PAD."""
+    _fields_ = [(n, ctypes.c_int) for n in ("BM", "BN", "BK", "TM", "TN", "PAD")]
+
+    def astuple(self):
+        return (self.BM, self.BN, self.BK, self.TM, self.TN, self.PAD)
+
+    def __repr__(self):
+        return "Tile(%d, %d, %d, %d, %d, %d)" % self.astuple()
+
+
+class Attr(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("regs", "local_bytes", "smem_bytes", "blocks_per_sm", "threads",
+                                            "grid", "num_sms")]
+
+    def asdict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+# Best-measured defaults per dtype (tensor path: BM=128, BN=256, BK=32 words, 4 stages,
+# raster group 16 M-blocks; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4).
+DEFAULT_TILES = {
+    "f32": (128, 128, 8, 8, 8, 4),
+    "bf16": (128, 256, 32, 4, 16, 0),
+    "e4m3": (128, 256, 32, 4, 16, 0),
+}
+
+
+class PFError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERROR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load libpf_b200.so (raises if it is missing: the CUDA path has no fallback)."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(f"{p} is missing: build it with `python -m ptxforge_b200.build` "
+                               "(there is no CPU fallback)")
+        lib = ctypes.CDLL(p)
+        vp, ip, i = ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_int
+        lib.pf_open.argtypes = [i, ctypes.POINTER(vp)]
+        lib.pf_close.argtypes = [vp]
+        lib.pf_prepare.argtypes = [vp, i, ctypes.POINTER(Tile), i, i, i]
+        lib.pf_bind.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
+        lib.pf_launch.argtypes = [vp, vp]
+        lib.pf_time.argtypes = [vp, i, i, i, ctypes.POINTER(ctypes.c_double)]
+        lib.pf_attrs.argtypes = [vp, ctypes.POINTER(Attr)]
+        lib.pf_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
+        lib.pf_set_wait_timeout.argtypes = [vp, ctypes.c_ulonglong]
+        lib.pf_last_error.argtypes = [vp]
+        lib.pf_last_error.restype = ctypes.c_char_p
+        lib.pf_run_host.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
+        lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
+        lib.pf_elem_bytes.argtypes = [i]
+        lib.pf_elem_bytes.restype = ctypes.c_size_t
+        lib.pf_out_bytes.argtypes = [i]
+        lib.pf_out_bytes.restype = ctypes.c_size_t
+        lib.pf_version.restype = ctypes.c_char_p
+        lib.pf_selftest_wait_timeout.argtypes = [vp, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
+        for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
+                     "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
+                     "pf_selftest_wait_timeout"):
+            getattr(lib, name).restype = ctypes.c_int
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def version() -> str:
+    return load_library().pf_version().decode()
+
+
+def shard_rows(M: int, G: int, g: int, align: int = 128) -> tuple[int, int]:
+    """Rows [row0, row0 + rows) of the M-row problem that shard g of G owns (pf_shard_rows)."""
+    r0, n = ctypes.c_int(), ctypes.c_int()
+    rc = load_library().pf_shard_rows(M, G, g, align, ctypes.byref(r0), ctypes.byref(n))
+    if rc:
+        raise PFError(rc, "pf_shard_rows: bad arguments")
+    return r0.value, n.value
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    if hasattr(x, "ctypes"):
+        return int(x.ctypes.data)
+    raise TypeError(f"cannot take a device/host pointer of {type(x)}")
+
+
+class Context:
+    """One pf_ctx: a GPU, a stream, a prepared kernel variant and bound operands."""
+
+    def __init__(self, device: int = 0):
+        self._lib = load_library()
+        h = ctypes.c_void_p()
+        rc = self._lib.pf_open(device, ctypes.byref(h))
+        if rc:
+            raise PFError(rc, f"pf_open(device={device}) failed: no sm_100 GPU visible, and this backend "
+                              "has no CPU fallback")
+        self._h = h
+        self.device = device
+        self.dtype = None
+        self.shape = None
+        self.tile = None
+
+    def _check(self, rc: int, what: str):
+        if rc:
+            raise PFError(rc, f"{what}: {self._lib.pf_last_error(self._h).decode()}")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.pf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def prepare(self, dtype: str, tile, M: int, N: int, K: int):
+        t = tile if isinstance(tile, Tile) else Tile(*(tile or DEFAULT_TILES[dtype]))
+        self._check(self._lib.pf_prepare(self._h, DTYPES[dtype], ctypes.byref(t), M, N, K), "pf_prepare")
+        self.dtype, self.shape, self.tile = dtype, (M, N, K), t
+        return self
+
+    def bind(self, A, B, bias, C, scale_a: float = 1.0, scale_b: float = 1.0):
+        self._check(self._lib.pf_bind(self._h, _ptr(A), _ptr(B), _ptr(bias), _ptr(C), scale_a, scale_b),
+                    "pf_bind")
+        return self
+
+    def launch(self, stream=None):
+        s = 0 if stream is None else (stream if isinstance(stream, int) else int(stream.cuda_stream))
+        self._check(self._lib.pf_launch(self._h, s), "pf_launch")
+
+    def time(self, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
+        ms = ctypes.c_double()
+        self._check(self._lib.pf_time(self._h, warmup, iters, reps, ctypes.byref(ms)), "pf_time")
+        return ms.value
+
+    def attrs(self) -> dict:
+        a = Attr()
+        self._check(self._lib.pf_attrs(self._h, ctypes.byref(a)), "pf_attrs")
+        return a.asdict()
+
+    def status(self) -> int:
+        w = ctypes.c_uint()
+        self._check(self._lib.pf_device_status(self._h, ctypes.byref(w)), "pf_device_status")
+        return w.value
+
+    def set_wait_timeout(self, ns: int):
+        self._check(self._lib.pf_set_wait_timeout(self._h, ns), "pf_set_wait_timeout")
+
+    def run_host(self, hA, hB, hbias, hC, scale_a: float = 1.0, scale_b: float = 1.0):
+        """H2D copies of host operands, launch, D2H of C, synchronise (pf_run_host)."""
+        self._check(self._lib.pf_run_host(self._h, _ptr(hA), _ptr(hB), _ptr(hbias), _ptr(hC), scale_a, scale_b),
+                    "pf_run_host")
+
+    def selftest_wait_timeout(self, ns: int) -> int:
+        w = ctypes.c_uint()
+        self._check(self._lib.pf_selftest_wait_timeout(self._h, ns, ctypes.byref(w)), "pf_selftest_wait_timeout")
+        return w.value
+
+
+_contexts: dict = {}
+
+
+def context(device: int = 0) -> Context:
+    """A cached Context per device for the convenience functions below."""
+    c = _contexts.get(device)
+    if c is None:
+        c = _contexts[device] = Context(device)
+    return c
+
+
+def gemm_bias_gelu(A, B, bias, C=None, *, dtype: str | None = None, tile=None, scale_a: float = 1.0,
+                   scale_b: float = 1.0, stream=None):
+    """C = gelu_tanh(scale_a*scale_b * A @ B + bias) for CUDA torch tensors (row-major, contiguous).
+
+    dtype: "f32" (A, B, C float32), "bf16" (A, B bfloat16, C bfloat16) or "e4m3" (A, B float8_e4m3fn or
+    uint8 codes, C bfloat16).  bias is float32 [N].  Returns C.
+    """
+    import torch
+
+    if dtype is None:
+        dtype = {torch.float32: "f32", torch.bfloat16: "bf16"}.get(A.dtype, "e4m3")
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K or bias.shape != (N,):
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}, bias {tuple(bias.shape)}")
+    for t in (A, B, bias):
+        if not t.is_cuda or not t.is_contiguous():
+            raise ValueError("operands must be contiguous CUDA tensors")
+    if bias.dtype != torch.float32:
+        raise ValueError("bias must be float32")
+    out_dtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    if C is None:
+        C = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    ctx = context(A.device.index or 0)
+    key = (dtype, tuple(tile) if tile else None, M, N, K)
+    if getattr(ctx, "_key", None) != key:
+        ctx.prepare(dtype, tile, M, N, K)
+        ctx._key = key
+    ctx.bind(A, B, bias, C, scale_a, scale_b)
+    if stream is None:
+        stream = torch.cuda.current_stream(A.device)
+    ctx.launch(stream)
+    return C

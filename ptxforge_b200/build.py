@@ -1,0 +1,73 @@
+"""Build recipe for the sm_100a shared library ``libpf_b200.so`` (the C ABI of include/pf_b200.h).
+
+    python -m ptxforge_b200.build            # builds in place, next to this file
+
+nvcc cross-compiles for sm_100a on a machine without a GPU.  The CUDA runtime is linked
+statically and the driver is reached through cudaGetDriverEntryPoint, so the library loads (and
+reports PF_ENODEV) where no GPU driver is installed.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+LIB = os.path.join(HERE, "libpf_b200.so")
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path() -> str:
+    cand = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    if os.path.exists(cand):
+        return cand
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found: set CUDA_HOME")
+    return found
+
+
+def _sources() -> list[str]:
+    out = []
+    for d in (CSRC, INCLUDE):
+        for name in sorted(os.listdir(d)):
+            if name.endswith((".cu", ".cuh", ".h", ".hpp")):
+                out.append(os.path.join(d, name))
+    return out
+
+
+def _stale(target: str, deps: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile libpf_b200.so if any source is newer than it; return its path."""
+    if not force and not _stale(LIB, _sources() + [os.path.abspath(__file__)]):
+        return LIB
+    cmd = [
+        nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
+        "-Xcompiler", "-fPIC,-Wall", "-shared", "-cudart", "static",
+        "-I", INCLUDE, "-I", CSRC, "-Xptxas", "-v",
+        os.path.join(CSRC, "pf_b200.cu"), "-o", LIB + ".tmp",
+    ]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    log = r.stdout + r.stderr
+    if r.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + log[-6000:])
+    os.replace(LIB + ".tmp", LIB)
+    with open(os.path.join(HERE, "libpf_b200.ptxas.txt"), "w") as f:
+        f.write(log)
+    if verbose:
+        print(log)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

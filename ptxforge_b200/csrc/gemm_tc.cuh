@@ -1,0 +1,335 @@
+// gemm_tc.cuh -- fused C = gelu_tanh(scale * A.B + bias) on the 5th-generation tensor cores.
+//
+// Persistent, warp-specialised kernel for sm_100a (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: one elected lane streams A (K-major) and B (N-major) k-blocks into a
+//               STAGES-deep ring of 128-byte-swizzled shared-memory tiles (full/empty mbarriers).
+//   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 bf16 /
+//               32 e4m3) into a double-buffered fp32 accumulator (2 x BN TMEM columns) and
+//               tcgen05.commit's the smem stage back to the producer and the finished accumulator
+//               to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, x*scale + bias[c], GELU(tanh form) with
+//               MUFU tanh, round to bf16, stage through swizzled shared memory and TMA-store; the
+//               pre-activation never touches HBM.  The accumulator buffer is handed back to the
+//               MMA warp right after its last TMEM load, so tile i's epilogue overlaps tile i+1's
+//               mainloop.
+//
+// Math is that of the reference kernel (kernels/gemm_bias_gelu.cu:37-40, 89-97): a row-major
+// GEMM over K followed by +bias[c] and gelu_tanh with k0 = 0.7978845608028654, k1 = 0.044715.
+// Inputs here are bf16 or e4m3 (the reference is fp32 only), accumulation is fp32 in TMEM.
+//
+// Shapes: any M >= 1; N and K as required by TMA row strides (multiples of 16 bytes).  Partial
+// tiles are handled by TMA: loads outside the tensor are zero-filled (contribute 0 to the dot
+// product) and stores outside it are clipped.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace pf {
+
+struct TcParams {
+  const float *bias;
+  float scale;             // scale_a * scale_b (1 for bf16)
+  int M, N, K;
+  int num_m_blocks, num_n_blocks, num_tiles, k_blocks;
+  int group_m;             // raster: tiles walk `group_m` M-blocks before moving to the next N-block
+  unsigned *status;        // device status word (bounded-wait timeouts)
+  unsigned long long timeout_ns;
+};
+
+// kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).
+template <int kDtype, int kBN, int kStages>
+struct TcConfig {
+  static constexpr int BM = 128;
+  static constexpr int BN = kBN;
+  static constexpr int STAGES = kStages;
+  static constexpr int ELEM = (kDtype == 0) ? 2 : 1;        // bytes per A/B element
+  static constexpr int BK = 128 / ELEM;                      // k elements per stage = one 128-B row
+  static constexpr int UMMA_K = 32 / ELEM;                   // k per tcgen05.mma
+  static constexpr int A_BYTES = BM * 128;                   // 128 rows x 128 B
+  static constexpr int B_CHUNK_N = 128 / ELEM;               // N elements per 128-B row of B
+  static constexpr int B_CHUNKS = BN / B_CHUNK_N;            // TMA boxes of B per stage
+  static constexpr int B_CHUNK_BYTES = BK * 128;             // BK rows x 128 B
+  static constexpr int B_BYTES = B_CHUNKS * B_CHUNK_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int EPI_COLS = 64;                        // bf16 output columns per TMA store box
+  static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;   // 32 rows x 128 B
+  static constexpr int EPI_BUFS = 2;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 192;
+  static constexpr uint32_t IDESC =
+      instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, /*A K-major*/ 0u, /*B MN-major*/ 1u, BM, BN);
+
+  static_assert(BN % B_CHUNK_N == 0, "BN must be a multiple of one 128-byte row of B");
+  static_assert(BN % EPI_COLS == 0, "BN must be a multiple of the epilogue store width");
+  static_assert(BN >= 16 && BN <= 256 && BN % 16 == 0, "UMMA N for M=128 is 16..256 in steps of 16");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
+};
+
+// Tile order: consecutive tile ids walk down `group_m` M-blocks, then across N, so the CTAs that
+// run at the same time share A row panels and B column panels in L2.
+__device__ __forceinline__ void tile_coords(int t, const TcParams &p, int &mb, int &nb) {
+  const int per_group = p.group_m * p.num_n_blocks;
+  const int g = t / per_group;
+  const int first_m = g * p.group_m;
+  const int rows = min(p.num_m_blocks - first_m, p.group_m);
+  const int r = t - g * per_group;
+  mb = first_m + r % rows;
+  nb = r / rows;
+}
+
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  // 0.5*x*(1 + tanh(k0*(x + k1*x^3))) with k0 = 0.7978845608028654, k1 = 0.044715.
+  const float k0 = 0.7978845608028654f, k0k1 = 0.7978845608028654f * 0.044715f;
+  const float x2 = x * x;
+  const float u = x * fmaf(k0k1, x2, k0);
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_approx(u), hx);
+}
+
+enum : unsigned {
+  kErrProducerWait = 1u,
+  kErrMmaWait = 2u,
+  kErrEpilogueWait = 4u,
+  kErrTeardownWait = 8u,
+};
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
+    gemm_bias_gelu_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled tiles need 1024-byte aligned shared addresses.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + Cfg::STAGES * Cfg::A_BYTES;
+  uint8_t *sEpi = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + Cfg::EPI_BYTES);
+  uint64_t *full = bars;                        // [STAGES] TMA bytes landed
+  uint64_t *empty = bars + Cfg::STAGES;         // [STAGES] MMAs reading the stage finished
+  uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [2] accumulator ready for the epilogue
+  uint64_t *tempty = tfull + 2;                 // [2] accumulator drained by the epilogue
+  uint64_t *drain = tempty + 2;                 // [1] teardown: all MMAs complete
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], Cfg::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  auto fail = [&](unsigned bit) {
+    atomicOr(p.status, bit);
+    *abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
+            fail(kErrProducerWait);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
+          uint8_t *b_dst = sB + stage * Cfg::B_BYTES;
+#pragma unroll
+          for (int j = 0; j < Cfg::B_CHUNKS; ++j)
+            tma_load_2d(b_dst + j * Cfg::B_CHUNK_BYTES, &tmB, &full[stage], nb * Cfg::BN + j * Cfg::B_CHUNK_N,
+                        kb * Cfg::BK);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Loads already issued must land before the block may exit: wait for each stage's last
+        // issued phase (bounded; the stage that failed was never issued).
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+          // stage s was last issued in phase (phase if s < stage else phase^1) -- only if issued.
+          const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+          volatile int no_abort = 0;
+          if (!mbar_wait(&full[s], ph, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+          fail(kErrMmaWait);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
+            fail(kErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+            // A: K-major, 128-B swizzle; k advances 32 bytes inside the swizzle row.
+            const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+            // B: N-major, 128-B swizzle; k advances UMMA_K rows of 128 B; LBO = next 128-B column chunk.
+            const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+            if constexpr (Cfg::ELEM == 2)
+              tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+            else
+              tc_mma_f8(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued must complete before TMEM is released.
+      tc_commit(drain);
+      volatile int no_abort = 0;
+      if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;                  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      // The TMEM loads below are warp-collective (.sync.aligned): the whole warp proceeds or leaves.
+      const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, waited)) {
+        if (lane == 0) fail(kErrEpilogueWait);
+        break;
+      }
+      tc_fence_after();
+      const int m0 = mb * Cfg::BM + q * 32;
+      const int n_tile = nb * Cfg::BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
+#pragma unroll 1
+      for (int c = 0; c < Cfg::BN / Cfg::EPI_COLS; ++c) {
+        const uint32_t sbuf = smem_u32(ebuf + buf * Cfg::EPI_BUF_BYTES) + lane * 128;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS + h * 32, v);
+          tmem_ld_wait();
+          const int n0 = n_tile + c * Cfg::EPI_COLS + h * 32;
+          uint32_t packed[16];
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
+            const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
+            const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
+            const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
+            const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
+            packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
+            packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
+          }
+          // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t chunk = static_cast<uint32_t>((h * 4 + i) ^ (lane & 7));
+            st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2],
+                         packed[i * 4 + 3]);
+          }
+        }
+        if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
+          // Last TMEM read of this accumulator: hand it back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, ebuf + buf * Cfg::EPI_BUF_BYTES, n_tile + c * Cfg::EPI_COLS, m0);
+          tma_store_commit();
+          tma_store_wait_read<1>();  // the other buffer is free again
+        }
+        __syncwarp();
+        buf ^= 1;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace pf

@@ -1,0 +1,591 @@
+// pf_b200.cu -- the C ABI declared in include/pf_b200.h.
+//
+// One pf_ctx per (host thread, GPU).  pf_prepare picks a kernel variant for (dtype, tile, M, N, K),
+// pf_bind records caller-owned device operands and encodes the TMA tensor maps, pf_launch launches,
+// pf_time applies the reference timing protocol (core/src/cuda_runner.cpp:110-130).
+//
+// The CUDA driver is reached only through the runtime (cudaGetDriverEntryPoint for
+// cuTensorMapEncodeTiled), so the library loads on a machine without a GPU driver; every entry
+// point then reports PF_ENODEV instead of failing to load.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "pf_b200.h"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+
+#ifndef PF_VERSION_STR
+#define PF_VERSION_STR "0.1.0"
+#endif
+
+namespace {
+
+using pf::TcConfig;
+using pf::TcParams;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+enum class Path { kNone, kSimt, kTensor };
+
+// Launch description of one compiled variant.
+struct Variant {
+  Path path = Path::kNone;
+  const void *func = nullptr;  // kernel symbol (for attributes / occupancy)
+  int threads = 0;
+  int smem = 0;                // dynamic shared memory
+  // tensor path
+  int bm = 0, bn = 0, bk_elems = 0, stages = 0, elem = 0;
+  int b_chunk_n = 0;
+  void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
+                    const TcParams &) = nullptr;
+  // simt path
+  int sbm = 0, sbn = 0;
+  void (*launch_simt)(dim3, cudaStream_t, const float *, const float *, const float *, float *, int, int, int,
+                      bool vec) = nullptr;
+};
+
+template <int DT, int BN, int ST>
+void launch_tc_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                    const TcParams &p) {
+  using Cfg = TcConfig<DT, BN, ST>;
+  pf::gemm_bias_gelu_tc<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+}
+
+template <int DT, int BN, int ST>
+Variant make_tc_variant() {
+  using Cfg = TcConfig<DT, BN, ST>;
+  Variant v;
+  v.path = Path::kTensor;
+  v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc<Cfg>);
+  v.threads = Cfg::THREADS;
+  v.smem = Cfg::SMEM_BYTES;
+  v.bm = Cfg::BM;
+  v.bn = Cfg::BN;
+  v.bk_elems = Cfg::BK;
+  v.stages = Cfg::STAGES;
+  v.elem = Cfg::ELEM;
+  v.b_chunk_n = Cfg::B_CHUNK_N;
+  v.launch_tc = &launch_tc_impl<DT, BN, ST>;
+  return v;
+}
+
+template <int BM, int BN, int BK, int TM, int TN, int PAD>
+void launch_simt_impl(dim3 grid, cudaStream_t s, const float *A, const float *B, const float *bias, float *C, int M,
+                      int N, int K, bool vec) {
+  using Cfg = pf::SimtConfig<BM, BN, BK, TM, TN, PAD>;
+  if (vec)
+    pf::gemm_bias_gelu_simt<BM, BN, BK, TM, TN, PAD, true><<<grid, Cfg::THREADS, 0, s>>>(A, B, bias, C, M, N, K);
+  else
+    pf::gemm_bias_gelu_simt<BM, BN, BK, TM, TN, PAD, false><<<grid, Cfg::THREADS, 0, s>>>(A, B, bias, C, M, N, K);
+}
+
+template <int BM, int BN, int BK, int TM, int TN, int PAD>
+Variant make_simt_variant() {
+  using Cfg = pf::SimtConfig<BM, BN, BK, TM, TN, PAD>;
+  Variant v;
+  v.path = Path::kSimt;
+  v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_simt<BM, BN, BK, TM, TN, PAD, true>);
+  v.threads = Cfg::THREADS;
+  v.smem = 0;
+  v.sbm = BM;
+  v.sbn = BN;
+  v.launch_simt = &launch_simt_impl<BM, BN, BK, TM, TN, PAD>;
+  return v;
+}
+
+struct SimtEntry {
+  pf_tile tile;
+  Variant (*make)();
+};
+
+// fp32 tile configs compiled into the library (the reference compiles one per trial with nvcc -D).
+const SimtEntry kSimtTable[] = {
+    {{128, 128, 8, 8, 8, 4}, &make_simt_variant<128, 128, 8, 8, 8, 4>},
+    {{128, 128, 8, 8, 8, 0}, &make_simt_variant<128, 128, 8, 8, 8, 0>},
+    {{128, 128, 16, 8, 8, 4}, &make_simt_variant<128, 128, 16, 8, 8, 4>},
+    {{128, 64, 8, 8, 4, 4}, &make_simt_variant<128, 64, 8, 8, 4, 4>},
+    {{64, 128, 8, 4, 8, 4}, &make_simt_variant<64, 128, 8, 4, 8, 4>},
+    {{64, 64, 8, 4, 4, 0}, &make_simt_variant<64, 64, 8, 4, 4, 0>},
+    {{64, 64, 8, 4, 4, 4}, &make_simt_variant<64, 64, 8, 4, 4, 4>},
+    {{64, 64, 16, 4, 4, 4}, &make_simt_variant<64, 64, 16, 4, 4, 4>},
+    {{32, 64, 8, 2, 4, 4}, &make_simt_variant<32, 64, 8, 2, 4, 4>},
+    {{32, 32, 8, 2, 2, 0}, &make_simt_variant<32, 32, 8, 2, 2, 0>},
+};
+
+bool same_tile(const pf_tile &a, const pf_tile &b) {
+  return a.BM == b.BM && a.BN == b.BN && a.BK == b.BK && a.TM == b.TM && a.TN == b.TN && a.PAD == b.PAD;
+}
+
+// Tensor-path variant for (dtype, BN, stages).
+bool find_tc_variant(pf_dtype dt, int bn, int stages, Variant *out) {
+  if (dt == PF_BF16) {
+    if (bn == 256 && stages == 4) { *out = make_tc_variant<0, 256, 4>(); return true; }
+    if (bn == 256 && stages == 2) { *out = make_tc_variant<0, 256, 2>(); return true; }
+    if (bn == 128 && stages == 4) { *out = make_tc_variant<0, 128, 4>(); return true; }
+    if (bn == 128 && stages == 2) { *out = make_tc_variant<0, 128, 2>(); return true; }
+    if (bn == 64 && stages == 8) { *out = make_tc_variant<0, 64, 8>(); return true; }
+    if (bn == 64 && stages == 4) { *out = make_tc_variant<0, 64, 4>(); return true; }
+  } else if (dt == PF_E4M3) {
+    if (bn == 256 && stages == 4) { *out = make_tc_variant<1, 256, 4>(); return true; }
+    if (bn == 256 && stages == 2) { *out = make_tc_variant<1, 256, 2>(); return true; }
+    if (bn == 128 && stages == 4) { *out = make_tc_variant<1, 128, 4>(); return true; }
+    if (bn == 128 && stages == 2) { *out = make_tc_variant<1, 128, 2>(); return true; }
+  }
+  return false;
+}
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+struct pf_ctx {
+  int device = -1;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  unsigned *d_status = nullptr;
+  unsigned long long timeout_ns = 4000000000ull;
+  std::string err;
+
+  bool prepared = false, bound = false;
+  pf_dtype dtype = PF_F32;
+  pf_tile tile{};
+  int M = 0, N = 0, K = 0;
+  Variant var;
+  int group_m = 16;
+
+  const void *A = nullptr, *B = nullptr;
+  const float *bias = nullptr;
+  void *C = nullptr;
+  float sa = 1.f, sb = 1.f;
+  CUtensorMap tmA{}, tmB{}, tmC{};
+  bool simt_vec = false;
+
+  // pf_run_host buffers
+  void *hbufA = nullptr, *hbufB = nullptr, *hbufC = nullptr;
+  float *hbufBias = nullptr;
+  size_t capA = 0, capB = 0, capC = 0, capBias = 0;
+
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+namespace {
+
+int set_err(pf_ctx *c, int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return code;
+}
+
+#define PF_CUDA(ctx, call)                                                                               \
+  do {                                                                                                   \
+    cudaError_t _e = (call);                                                                             \
+    if (_e != cudaSuccess) return set_err(ctx, PF_ECUDA, "%s -> %s", #call, cudaGetErrorString(_e));    \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int encode_2d(pf_ctx *c, CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_err(c, PF_ECUDA, "cuTensorMapEncodeTiled unavailable from the CUDA driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_err(c, PF_ECUDA, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu tensor, box %ux%u", (int)r,
+                   (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+  return PF_OK;
+}
+
+int encode_maps(pf_ctx *c) {
+  const Variant &v = c->var;
+  const CUtensorMapDataType in_t =
+      (c->dtype == PF_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t e = static_cast<uint64_t>(v.elem);
+  int rc;
+  // A: [M x K], K contiguous; box = BK elements (128 B) x BM rows.
+  rc = encode_2d(c, &c->tmA, in_t, c->A, c->K, c->M, c->K * e, v.bk_elems, v.bm, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // B: [K x N], N contiguous; box = 128 B of N x BK rows.
+  rc = encode_2d(c, &c->tmB, in_t, c->B, c->N, c->K, c->N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // C: [M x N] bf16; box = 64 columns (128 B) x 32 rows (one epilogue warp).
+  rc = encode_2d(c, &c->tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c->C, c->N, c->M, c->N * 2ull, 64, 32,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  return rc;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int do_launch(pf_ctx *c, cudaStream_t s) {
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_launch before pf_prepare");
+  if (!c->bound) return set_err(c, PF_ESTATE, "pf_launch before pf_bind");
+  const Variant &v = c->var;
+  if (v.path == Path::kTensor) {
+    TcParams p;
+    p.bias = c->bias;
+    p.scale = c->sa * c->sb;
+    p.M = c->M;
+    p.N = c->N;
+    p.K = c->K;
+    p.num_m_blocks = (c->M + v.bm - 1) / v.bm;
+    p.num_n_blocks = (c->N + v.bn - 1) / v.bn;
+    p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+    p.k_blocks = (c->K + v.bk_elems - 1) / v.bk_elems;
+    p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
+    p.status = c->d_status;
+    p.timeout_ns = c->timeout_ns;
+    dim3 grid(std::min(p.num_tiles, c->num_sms));
+    v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, p);
+  } else {
+    dim3 grid((c->N + v.sbn - 1) / v.sbn, (c->M + v.sbm - 1) / v.sbm);
+    v.launch_simt(grid, s, static_cast<const float *>(c->A), static_cast<const float *>(c->B), c->bias,
+                  static_cast<float *>(c->C), c->M, c->N, c->K, c->simt_vec);
+  }
+  PF_CUDA(c, cudaGetLastError());
+  return PF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *pf_version(void) { return "ptxforge_b200 " PF_VERSION_STR " (sm_100a)"; }
+
+size_t pf_elem_bytes(pf_dtype dt) {
+  switch (dt) {
+    case PF_F32:
+    case PF_F32_3XTF32: return 4;
+    case PF_BF16: return 2;
+    case PF_E4M3: return 1;
+  }
+  return 0;
+}
+
+size_t pf_out_bytes(pf_dtype dt) {
+  switch (dt) {
+    case PF_F32:
+    case PF_F32_3XTF32: return 4;
+    case PF_BF16:
+    case PF_E4M3: return 2;
+  }
+  return 0;
+}
+
+int pf_open(int device, pf_ctx **out) {
+  if (!out) return PF_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return PF_ENODEV;
+  }
+  if (device < 0 || device >= n) return PF_ENODEV;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PF_ENODEV;
+  if (prop.major != 10) return PF_ENODEV;  // kernels are sm_100a only
+  pf_ctx *c = new pf_ctx();
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  DeviceGuard g(device);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->d_status, sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c->d_status, 0, sizeof(unsigned)) != cudaSuccess || cudaEventCreate(&c->ev0) != cudaSuccess ||
+      cudaEventCreate(&c->ev1) != cudaSuccess) {
+    pf_close(c);
+    return PF_ECUDA;
+  }
+  *out = c;
+  return PF_OK;
+}
+
+int pf_close(pf_ctx *c) {
+  if (!c) return PF_EINVAL;
+  if (c->device >= 0) {
+    DeviceGuard g(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->d_status) cudaFree(c->d_status);
+    if (c->hbufA) cudaFree(c->hbufA);
+    if (c->hbufB) cudaFree(c->hbufB);
+    if (c->hbufC) cudaFree(c->hbufC);
+    if (c->hbufBias) cudaFree(c->hbufBias);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
+    if (c->stream) cudaStreamDestroy(c->stream);
+  }
+  delete c;
+  return PF_OK;
+}
+
+const char *pf_last_error(const pf_ctx *c) { return c ? c->err.c_str() : "null context"; }
+
+int pf_set_wait_timeout(pf_ctx *c, unsigned long long ns) {
+  if (!c || ns == 0) return set_err(c, PF_EINVAL, "timeout must be positive");
+  c->timeout_ns = ns;
+  return PF_OK;
+}
+
+int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
+  if (!c || !t) return set_err(c, PF_EINVAL, "null argument");
+  c->prepared = false;
+  c->bound = false;
+  if (M <= 0 || N <= 0 || K <= 0) return set_err(c, PF_EINVAL, "M, N, K must be positive (got %d, %d, %d)", M, N, K);
+  DeviceGuard g(c->device);
+  Variant v;
+  if (dt == PF_F32) {
+    bool found = false;
+    for (const SimtEntry &e : kSimtTable)
+      if (same_tile(e.tile, *t)) {
+        v = e.make();
+        found = true;
+        break;
+      }
+    if (!found)
+      return set_err(c, PF_ETILE, "fp32 tile %dx%dx%d t%dx%d p%d is not compiled into this library", t->BM, t->BN,
+                     t->BK, t->TM, t->TN, t->PAD);
+  } else if (dt == PF_BF16 || dt == PF_E4M3) {
+    if (t->BM != 128) return set_err(c, PF_ETILE, "tensor path: BM must be 128 (one CTA, UMMA M=128), got %d", t->BM);
+    if (t->BK != 32)
+      return set_err(c, PF_ETILE, "tensor path: BK must be 32 words (one 128-byte swizzle row), got %d", t->BK);
+    if (t->PAD != 0) return set_err(c, PF_ETILE, "tensor path: PAD must be 0, got %d", t->PAD);
+    if (t->TN < 1 || t->TN > 64) return set_err(c, PF_ETILE, "tensor path: TN (raster group) out of range: %d", t->TN);
+    if (!find_tc_variant(dt, t->BN, t->TM, &v))
+      return set_err(c, PF_ETILE, "tensor path: no %s kernel with BN=%d and %d stages", dt == PF_BF16 ? "bf16" : "e4m3",
+                     t->BN, t->TM);
+    const int e = (int)pf_elem_bytes(dt);
+    if ((static_cast<long long>(K) * e) % 16 != 0)
+      return set_err(c, PF_ESHAPE, "tensor path: rows of A must be a multiple of 16 bytes (K=%d)", K);
+    if ((static_cast<long long>(N) * e) % 16 != 0 || (N * 2) % 16 != 0)
+      return set_err(c, PF_ESHAPE, "tensor path: rows of B and C must be multiples of 16 bytes (N=%d)", N);
+    c->group_m = t->TN;
+  } else {
+    return set_err(c, PF_ETILE, "dtype %d is not built in this library", (int)dt);
+  }
+  if (v.path == Path::kTensor) {
+    cudaError_t e = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
+    if (e != cudaSuccess) return set_err(c, PF_ECUDA, "cudaFuncSetAttribute -> %s", cudaGetErrorString(e));
+  }
+  c->var = v;
+  c->dtype = dt;
+  c->tile = *t;
+  c->M = M;
+  c->N = N;
+  c->K = K;
+  c->prepared = true;
+  c->err.clear();
+  return PF_OK;
+}
+
+int pf_bind(pf_ctx *c, const void *A, const void *B, const float *bias, void *C, float sa, float sb) {
+  if (!c) return PF_EINVAL;
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_bind before pf_prepare");
+  if (!A || !B || !bias || !C) return set_err(c, PF_EINVAL, "null operand");
+  if (c->dtype != PF_E4M3 && (sa != 1.f || sb != 1.f))
+    return set_err(c, PF_EINVAL, "scales apply to e4m3 operands only (got %g, %g)", sa, sb);
+  DeviceGuard g(c->device);
+  c->bound = false;
+  c->A = A;
+  c->B = B;
+  c->bias = bias;
+  c->C = C;
+  c->sa = sa;
+  c->sb = sb;
+  if (c->var.path == Path::kTensor) {
+    if (!aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(bias))
+      return set_err(c, PF_EINVAL, "tensor path: operands must be 16-byte aligned");
+    int rc = encode_maps(c);
+    if (rc) return rc;
+  } else {
+    c->simt_vec = aligned16(A) && aligned16(B) && aligned16(C) && aligned16(bias) && (c->K % 4 == 0) &&
+                  (c->N % 4 == 0);
+  }
+  c->bound = true;
+  return PF_OK;
+}
+
+int pf_launch(pf_ctx *c, void *stream) {
+  if (!c) return PF_EINVAL;
+  DeviceGuard g(c->device);
+  return do_launch(c, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+}
+
+int pf_time(pf_ctx *c, int warmup, int iters, int reps, double *median_ms) {
+  if (!c || !median_ms || warmup < 0 || iters <= 0 || reps <= 0) return set_err(c, PF_EINVAL, "bad timing arguments");
+  DeviceGuard g(c->device);
+  int rc;
+  for (int i = 0; i < warmup; ++i)
+    if ((rc = do_launch(c, c->stream))) return rc;
+  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  std::vector<double> per;
+  for (int r = 0; r < reps; ++r) {
+    PF_CUDA(c, cudaEventRecord(c->ev0, c->stream));
+    for (int i = 0; i < iters; ++i)
+      if ((rc = do_launch(c, c->stream))) return rc;
+    PF_CUDA(c, cudaEventRecord(c->ev1, c->stream));
+    PF_CUDA(c, cudaEventSynchronize(c->ev1));
+    float ms = 0.f;
+    PF_CUDA(c, cudaEventElapsedTime(&ms, c->ev0, c->ev1));
+    per.push_back(static_cast<double>(ms) / iters);
+  }
+  std::sort(per.begin(), per.end());
+  *median_ms = per[per.size() / 2];
+  unsigned st = 0;
+  PF_CUDA(c, cudaMemcpy(&st, c->d_status, sizeof st, cudaMemcpyDeviceToHost));
+  if (st) return set_err(c, PF_ETIMEOUT, "a bounded device wait ran out during timing (status 0x%x)", st);
+  return PF_OK;
+}
+
+int pf_attrs(pf_ctx *c, pf_attr *out) {
+  if (!c || !out) return PF_EINVAL;
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_attrs before pf_prepare");
+  DeviceGuard g(c->device);
+  cudaFuncAttributes fa;
+  PF_CUDA(c, cudaFuncGetAttributes(&fa, c->var.func));
+  int bps = 0;
+  PF_CUDA(c, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, c->var.func, c->var.threads, c->var.smem));
+  out->regs = fa.numRegs;
+  out->local_bytes = static_cast<int>(fa.localSizeBytes);
+  out->smem_bytes = static_cast<int>(fa.sharedSizeBytes) + c->var.smem;
+  out->blocks_per_sm = bps;
+  out->threads = c->var.threads;
+  out->num_sms = c->num_sms;
+  if (c->var.path == Path::kTensor) {
+    const int tiles = ((c->M + c->var.bm - 1) / c->var.bm) * ((c->N + c->var.bn - 1) / c->var.bn);
+    out->grid = std::min(tiles, c->num_sms);
+  } else {
+    out->grid = ((c->N + c->var.sbn - 1) / c->var.sbn) * ((c->M + c->var.sbm - 1) / c->var.sbm);
+  }
+  return PF_OK;
+}
+
+int pf_device_status(pf_ctx *c, unsigned *err_word) {
+  if (!c || !err_word) return PF_EINVAL;
+  DeviceGuard g(c->device);
+  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  PF_CUDA(c, cudaMemcpy(err_word, c->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  PF_CUDA(c, cudaMemset(c->d_status, 0, sizeof(unsigned)));
+  return PF_OK;
+}
+
+int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, void *hC, float sa, float sb) {
+  if (!c) return PF_EINVAL;
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_run_host before pf_prepare");
+  if (!hA || !hB || !hbias || !hC) return set_err(c, PF_EINVAL, "null host operand");
+  DeviceGuard g(c->device);
+  const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
+  const size_t nA = static_cast<size_t>(c->M) * c->K * e, nB = static_cast<size_t>(c->K) * c->N * e;
+  const size_t nC = static_cast<size_t>(c->M) * c->N * o, nBias = static_cast<size_t>(c->N) * sizeof(float);
+  auto ensure = [&](void **buf, size_t *cap, size_t need) -> int {
+    if (*cap >= need) return PF_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    if (cudaMalloc(buf, need) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, PF_ENOMEM, "cudaMalloc(%zu) failed", need);
+    }
+    *cap = need;
+    return PF_OK;
+  };
+  int rc;
+  if ((rc = ensure(&c->hbufA, &c->capA, nA)) || (rc = ensure(&c->hbufB, &c->capB, nB)) ||
+      (rc = ensure(&c->hbufC, &c->capC, nC)) ||
+      (rc = ensure(reinterpret_cast<void **>(&c->hbufBias), &c->capBias, nBias)))
+    return rc;
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufA, hA, nA, cudaMemcpyHostToDevice, c->stream));
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufB, hB, nB, cudaMemcpyHostToDevice, c->stream));
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufBias, hbias, nBias, cudaMemcpyHostToDevice, c->stream));
+  if (!c->bound || c->A != c->hbufA || c->B != c->hbufB || c->C != c->hbufC || c->bias != c->hbufBias ||
+      c->sa != sa || c->sb != sb) {
+    if ((rc = pf_bind(c, c->hbufA, c->hbufB, c->hbufBias, c->hbufC, sa, sb))) return rc;
+  }
+  if ((rc = do_launch(c, c->stream))) return rc;
+  PF_CUDA(c, cudaMemcpyAsync(hC, c->hbufC, nC, cudaMemcpyDeviceToHost, c->stream));
+  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  return PF_OK;
+}
+
+int pf_shard_rows(int M, int G, int g, int align, int *row0, int *rows) {
+  if (M <= 0 || G <= 0 || g < 0 || g >= G || align <= 0 || !row0 || !rows) return PF_EINVAL;
+  // Split M into `blocks` units of `align` rows, spread as evenly as possible; the remainder rows of
+  // a ragged M go to the last shard.
+  const long long blocks = M / align;
+  const long long lo = blocks * g / G, hi = blocks * (g + 1) / G;
+  long long r0 = lo * align, r1 = hi * align;
+  if (g == G - 1) r1 = M;
+  *row0 = static_cast<int>(r0);
+  *rows = static_cast<int>(r1 - r0);
+  return PF_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Bounded-wait self-test: one block waits on an mbarrier that nothing arrives at.
+// ------------------------------------------------------------------------------------------------
+namespace {
+__global__ void selftest_wait_kernel(unsigned *status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    pf::mbar_init(&bar, 1);
+    abort_flag = 0;
+    pf::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!pf::mbar_wait(&bar, 0, timeout_ns, &abort_flag)) atomicOr(status, pf::kErrEpilogueWait);
+  }
+  __syncthreads();
+}
+}  // namespace
+
+extern "C" int pf_selftest_wait_timeout(pf_ctx *c, unsigned long long timeout_ns, unsigned *err_word) {
+  if (!c || !err_word || timeout_ns == 0 || timeout_ns > 10000000000ull)
+    return set_err(c, PF_EINVAL, "bad self-test arguments");
+  DeviceGuard g(c->device);
+  PF_CUDA(c, cudaMemsetAsync(c->d_status, 0, sizeof(unsigned), c->stream));
+  selftest_wait_kernel<<<1, 32, 0, c->stream>>>(c->d_status, timeout_ns);
+  PF_CUDA(c, cudaGetLastError());
+  return pf_device_status(c, err_word);
+}

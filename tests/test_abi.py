@@ -1,0 +1,73 @@
+"""The C-ABI library loads without a GPU and exports exactly what include/pf_b200.h declares (CPU only)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    text = open(os.path.join(ROOT, "include", "pf_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pf_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_matches_python_symbol_list(pf):
+    assert declared_functions() == sorted(pf.SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(pf):
+    lib = ctypes.CDLL(pf.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_sizes(pf):
+    assert "sm_100a" in pf.version()
+    lib = pf.load_library()
+    assert [lib.pf_elem_bytes(d) for d in (0, 1, 2, 3)] == [4, 4, 2, 1]
+    assert [lib.pf_out_bytes(d) for d in (0, 1, 2, 3)] == [4, 4, 2, 2]
+    assert lib.pf_elem_bytes(99) == 0
+
+
+def test_null_arguments_are_errors_not_crashes(pf):
+    lib = pf.load_library()
+    assert lib.pf_open(0, None) == pf.PF_EINVAL
+    assert lib.pf_close(None) == pf.PF_EINVAL
+    assert lib.pf_prepare(None, 2, None, 1, 1, 1) == pf.PF_EINVAL
+    assert lib.pf_launch(None, None) == pf.PF_EINVAL
+    assert lib.pf_last_error(None) == b"null context"
+
+
+def test_open_without_gpu_reports_nodev(pf):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    with pytest.raises(pf.PFError) as e:
+        pf.Context(0)
+    assert e.value.code == pf.PF_ENODEV
+
+
+@pytest.mark.parametrize("M,G,align", [(8192, 1, 128), (8192, 2, 128), (8192, 8, 128), (16384, 8, 128),
+                                       (1000, 3, 128), (100, 8, 128), (8192, 7, 128), (5, 2, 1)])
+def test_shard_rows_partition(pf, M, G, align):
+    spans = [pf.shard_rows(M, G, g, align) for g in range(G)]
+    pos = 0
+    for g, (r0, n) in enumerate(spans):
+        assert r0 == pos and n >= 0
+        if g < G - 1:
+            assert r0 % align == 0 and (r0 + n) % align == 0
+        pos += n
+    assert pos == M
+    sizes = [n for _, n in spans[:-1]]
+    if sizes and M >= align * G:
+        assert max(sizes) - min(sizes) <= align
+
+
+def test_shard_rows_rejects_bad_arguments(pf):
+    with pytest.raises(pf.PFError):
+        pf.shard_rows(100, 2, 2)
+    with pytest.raises(pf.PFError):
+        pf.shard_rows(0, 1, 0)

@@ -1,0 +1,269 @@
+"""Parity of the sm_100a kernels with the oracle, through the C ABI (needs a B200: -m gpu).
+
+Bars (BASELINE tolerances, metric max |ref - C| / (1 + |ref|) against fp64 of the (dequantised)
+inputs, the reference gate's metric core/src/cuda_runner.cpp:196):
+    fp32  1e-5        bf16  2e-2        e4m3  5e-2
+plus: the fp32 path is bit-identical to the reference's own kernel (kernels/gemm_bias_gelu.cu built for
+sm_100a, oracle/_ref/), and at the full BASELINE sizes every output is compared with a plain PyTorch
+fp32 computation of the same op (TF32 off) and the reference gate's 512 sampled fp64 points.
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from ptxforge_b200 import workloads as wl  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f32": 1e-5, "bf16": 2e-2, "e4m3": 5e-2}
+
+
+def _dev(x: np.ndarray, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    if dtype is torch.bfloat16:
+        t = t.view(torch.int16).view(torch.bfloat16)
+    elif dtype is torch.float8_e4m3fn:
+        t = t.view(torch.float8_e4m3fn)
+    return t
+
+
+def device_operands(w, inp):
+    if w.dtype == "f32":
+        A, B = _dev(inp.A_raw), _dev(inp.B_raw)
+        C = torch.full((w.M, w.N), float("nan"), device="cuda", dtype=torch.float32)
+    elif w.dtype == "bf16":
+        A, B = _dev(inp.A_raw.view(np.int16), torch.bfloat16), _dev(inp.B_raw.view(np.int16), torch.bfloat16)
+        C = torch.full((w.M, w.N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    else:
+        A, B = _dev(inp.A_raw, torch.float8_e4m3fn), _dev(inp.B_raw, torch.float8_e4m3fn)
+        C = torch.full((w.M, w.N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    return A, B, _dev(inp.bias), C
+
+
+def run_pf(ctx, w, inp, tile=None, ops=None):
+    A, B, bias, C = ops or device_operands(w, inp)
+    ctx.prepare(w.dtype, tile, w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C, inp.scale_a, inp.scale_b)
+    ctx.launch(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert ctx.status() == 0
+    return C
+
+
+def to_np(C):
+    return C.float().cpu().numpy()
+
+
+def check_full(oracle_mod, w, inp, C):
+    ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias, inp.scale_a * inp.scale_b)
+    Cn = to_np(C)
+    assert int(np.isnan(Cn).sum()) == 0, "unwritten outputs"
+    err = oracle_mod.max_rel_err(ref, Cn)
+    assert err <= TOL[w.dtype], f"{w.name} {w.M}x{w.N}x{w.K}: max rel err {err:.3e} > {TOL[w.dtype]}"
+    return err
+
+
+def torch_fp32_reference(A, B, bias, scale):
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        x = torch.matmul(A.float(), B.float())
+        if scale != 1.0:
+            x.mul_(scale)
+        x.add_(bias)
+        return torch.nn.functional.gelu(x, approximate="tanh")
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def max_rel_err_t(ref, C):
+    r = ref.double()
+    return float(((r - C.double()).abs() / (1.0 + r.abs())).max())
+
+
+# ---------------------------------------------------------------------------------------------
+# fp32 (SIMT) path
+# ---------------------------------------------------------------------------------------------
+FP32_TILES = [(128, 128, 8, 8, 8, 4), (128, 128, 8, 8, 8, 0), (128, 128, 16, 8, 8, 4), (128, 64, 8, 8, 4, 4),
+              (64, 128, 8, 4, 8, 4), (64, 64, 8, 4, 4, 0), (64, 64, 8, 4, 4, 4), (64, 64, 16, 4, 4, 4),
+              (32, 64, 8, 2, 4, 4), (32, 32, 8, 2, 2, 0)]
+
+
+@pytest.mark.parametrize("tile", FP32_TILES)
+def test_fp32_cfg1_every_tile(ctx, oracle_mod, tile):
+    w = wl.CONFIGS["cfg1_f32_512"]
+    inp = wl.make_inputs(w)
+    check_full(oracle_mod, w, inp, run_pf(ctx, w, inp, tile))
+
+
+@pytest.mark.parametrize("shape", [(200, 136, 72), (1, 8, 4), (129, 257, 33), (77, 5, 9)])
+def test_fp32_ragged_shapes(ctx, oracle_mod, shape):
+    w = wl.scaled(wl.CONFIGS["cfg1_f32_512"], *shape)
+    inp = wl.make_inputs(w, seed=7)
+    for tile in [(128, 128, 8, 8, 8, 4), (64, 64, 8, 4, 4, 0)]:
+        check_full(oracle_mod, w, inp, run_pf(ctx, w, inp, tile))
+
+
+@pytest.mark.parametrize("ref_name", ["default", "best5050"])
+def test_fp32_bit_identical_to_reference_kernel(ctx, oracle_mod, ref_name):
+    path = oracle_mod.ref_kernel_path(ref_name)
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref not built (needs the reference tree at build time)")
+    ref = oracle_mod.ref_kernel(ref_name)
+    for w in (wl.CONFIGS["cfg1_f32_512"], wl.CONFIGS["cfg2_f32_2048"]):
+        inp = wl.make_inputs(w)
+        A, B, bias, C = device_operands(w, inp)
+        C_ref = torch.full_like(C, float("nan"))
+        rc = ref.ref_launch(A.data_ptr(), B.data_ptr(), bias.data_ptr(), C_ref.data_ptr(), w.M, w.N, w.K,
+                            torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        mine = run_pf(ctx, w, inp, None, (A, B, bias, C))
+        torch.cuda.synchronize()
+        assert torch.equal(mine, C_ref), f"{w.name}: differs from the reference kernel ({ref_name})"
+
+
+def test_fp32_cfg2_gate_and_torch(ctx, oracle_mod):
+    w = wl.CONFIGS["cfg2_f32_2048"]
+    inp = wl.make_inputs(w)
+    A, B, bias, C = device_operands(w, inp)
+    run_pf(ctx, w, inp, None, (A, B, bias, C))
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= 1e-5
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= 1e-5
+
+
+# ---------------------------------------------------------------------------------------------
+# bf16 / e4m3 tensor-core path
+# ---------------------------------------------------------------------------------------------
+BF16_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
+              (128, 128, 32, 2, 8, 0), (128, 64, 32, 8, 16, 0), (128, 64, 32, 4, 2, 0)]
+E4M3_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
+              (128, 128, 32, 2, 4, 0)]
+
+
+@pytest.mark.parametrize("tile", BF16_TILES)
+@pytest.mark.parametrize("shape", [(256, 512, 320), (200, 136, 72), (128, 256, 64), (1, 8, 8), (300, 1000, 1000)])
+def test_bf16_small_vs_oracle(ctx, oracle_mod, tile, shape):
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], *shape)
+    inp = wl.make_inputs(w, seed=3)
+    check_full(oracle_mod, w, inp, run_pf(ctx, w, inp, tile))
+
+
+@pytest.mark.parametrize("tile", E4M3_TILES)
+@pytest.mark.parametrize("shape", [(256, 512, 512), (200, 144, 80), (1, 16, 16), (384, 1024, 768)])
+def test_e4m3_small_vs_oracle(ctx, oracle_mod, tile, shape):
+    w = wl.scaled(wl.CONFIGS["cfg5_e4m3_16384"], *shape)
+    inp = wl.make_inputs(w, seed=5)
+    check_full(oracle_mod, w, inp, run_pf(ctx, w, inp, tile))
+
+
+def test_mlp_shape_small_vs_oracle(ctx, oracle_mod):
+    w = wl.scaled(wl.CONFIGS["cfg4_bf16_mlp"], 512, 1792, 512)
+    inp = wl.make_inputs(w)
+    check_full(oracle_mod, w, inp, run_pf(ctx, w, inp))
+
+
+@pytest.mark.parametrize("name", ["cfg3_bf16_8192", "cfg4_bf16_mlp", "cfg5_e4m3_16384"])
+def test_full_size_gate_torch_and_determinism(ctx, oracle_mod, name):
+    w = wl.CONFIGS[name]
+    inp = wl.make_inputs(w)
+    ops = device_operands(w, inp)
+    A, B, bias, C = ops
+    run_pf(ctx, w, inp, None, ops)
+    Cn = to_np(C)
+    assert int(np.isnan(Cn).sum()) == 0
+    scale = inp.scale_a * inp.scale_b
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, Cn, scale=scale, samples=512, seed=99)
+    assert err <= TOL[w.dtype], f"sampled gate {err:.3e}"
+    ref = torch_fp32_reference(A, B, bias, scale)
+    e2 = max_rel_err_t(ref, C)
+    del ref
+    assert e2 <= TOL[w.dtype], f"full-matrix error vs torch fp32 {e2:.3e}"
+    # a second launch is bit-identical
+    C2 = torch.full_like(C, float("nan"))
+    run_pf(ctx, w, inp, None, (A, B, bias, C2))
+    assert torch.equal(C, C2)
+
+
+@pytest.mark.parametrize("G", [2, 3, 8])
+def test_row_shards_equal_unsharded(ctx, pf, G):
+    # Row sharding (the multi-GPU decomposition) on one GPU: each shard is its own launch on a row
+    # window of A and C; the concatenation is bit-identical to the single launch.
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 2048, 1024, 768)
+    inp = wl.make_inputs(w, seed=9)
+    A, B, bias, C = device_operands(w, inp)
+    run_pf(ctx, w, inp, None, (A, B, bias, C))
+    Cs = torch.full_like(C, float("nan"))
+    for g in range(G):
+        r0, n = pf.shard_rows(w.M, G, g, 128)
+        if n == 0:
+            continue
+        ctx.prepare("bf16", None, n, w.N, w.K)
+        ctx.bind(A[r0:r0 + n], B, bias, Cs[r0:r0 + n])
+        ctx.launch(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert ctx.status() == 0
+    assert torch.equal(C, Cs)
+
+
+def test_run_host_equals_device_path(ctx, pf):
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 384, 512, 256)
+    inp = wl.make_inputs(w, seed=2)
+    C = run_pf(ctx, w, inp)
+    hC = np.empty((w.M, w.N), dtype=np.uint16)
+    ctx.prepare("bf16", None, w.M, w.N, w.K)
+    ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC)
+    assert np.array_equal(hC, C.view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def test_timing_protocol_and_attrs(ctx):
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 1024, 1024, 1024)
+    inp = wl.make_inputs(w)
+    run_pf(ctx, w, inp)
+    ms = ctx.time(warmup=2, iters=5, reps=3)
+    assert 0 < ms < 50
+    a = ctx.attrs()
+    assert a["threads"] == 192 and a["blocks_per_sm"] == 1 and a["local_bytes"] == 0
+    assert a["num_sms"] == 148 and a["grid"] == min(a["num_sms"], (1024 // 128) * (1024 // 256))
+
+
+def test_invalid_configs_are_errors(ctx, pf):
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare("bf16", (64, 256, 32, 4, 16, 0), 256, 256, 256)
+    assert e.value.code == pf.PF_ETILE
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare("bf16", (128, 256, 32, 16, 16, 0), 256, 256, 256)
+    assert e.value.code == pf.PF_ETILE
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare("bf16", None, 256, 100, 256)  # 200-byte rows of B and C: not a TMA row
+    assert e.value.code == pf.PF_ESHAPE
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare("f32", (256, 256, 32, 16, 16, 8), 256, 256, 256)
+    assert e.value.code == pf.PF_ETILE
+    ctx.prepare("bf16", None, 256, 256, 256)
+    with pytest.raises(pf.PFError) as e:
+        ctx.launch()
+    assert e.value.code == pf.PF_ESTATE
+
+
+def test_bounded_wait_times_out_and_context_survives(ctx, oracle_mod):
+    # A wait on an mbarrier that nothing arrives at runs out after 20 ms; the kernel records it and
+    # returns, and the context keeps working.
+    assert ctx.selftest_wait_timeout(20_000_000) != 0
+    assert ctx.status() == 0
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 256, 256, 256)
+    inp = wl.make_inputs(w)
+    check_full(oracle_mod, w, inp, run_pf(ctx, w, inp))
+
+
+def test_torch_convenience_api(pf):
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 256, 512, 128)
+    inp = wl.make_inputs(w)
+    A, B, bias, _ = device_operands(w, inp)
+    C = pf.gemm_bias_gelu(A, B, bias)
+    torch.cuda.synchronize()
+    ref = torch_fp32_reference(A, B, bias, 1.0)
+    assert max_rel_err_t(ref, C) <= 2e-2
