@@ -56,8 +56,9 @@ typedef enum {
 /* The tuner's tile config: exactly the fields of ptxforge::Config (core/include/ptxforge/space.hpp:58).
  *   fp32 path   : the reference meaning (block tile BM x BN, K step BK, TM x TN per thread, PAD).
  *   tensor path : BM = CTA rows (128), BN = UMMA N (64/128/256), BK = K-block in 4-byte words
- *                 (32 = one 128-byte swizzle row), TM = smem pipeline stages, TN = epilogue column
- *                 chunks per TMEM load group, PAD = tile-raster group height in M blocks (0 = 16). */
+ *                 (32 = one 128-byte swizzle row), TM = smem pipeline stages, TN = tile-raster group
+ *                 height in M blocks (consecutive tiles walk TN row blocks before moving along N),
+ *                 PAD = 0. */
 typedef struct {
   int BM, BN, BK, TM, TN, PAD;
 } pf_tile;
@@ -99,8 +100,9 @@ int pf_prepare(pf_ctx *ctx, pf_dtype dtype, const pf_tile *tile, int M, int N, i
 int pf_bind(pf_ctx *ctx, const void *A, const void *B, const float *bias, void *C, float scale_a,
             float scale_b);
 
-/* Launch once on `stream` (a cudaStream_t; NULL = the context's own stream).  Asynchronous.
- * Replaces the cuLaunchKernel of cuda_runner.cpp:183. */
+/* Launch once on `stream` (a cudaStream_t; NULL = the CUDA default stream, where the reference
+ * launches, cuda_runner.cpp:183).  Asynchronous.  pf_time and pf_run_host use the context's own
+ * stream instead. */
 int pf_launch(pf_ctx *ctx, void *stream);
 
 /* Reference timing protocol (CudaRunner::Impl::median_ms, cuda_runner.cpp:110-130): `warmup`
@@ -111,7 +113,7 @@ int pf_time(pf_ctx *ctx, int warmup, int iters, int reps, double *median_ms);
 /* Kernel attributes of the prepared variant. */
 int pf_attrs(pf_ctx *ctx, pf_attr *out);
 
-/* Synchronise the context's stream and read (then clear) the device status word: 0 = clean,
+/* Synchronise the device and read (then clear) the context's device status word: 0 = clean,
  * nonzero = a bounded device-side wait ran out (bit 0: TMA-producer wait, bit 1: MMA wait,
  * bit 2: epilogue wait, bit 3: teardown wait). */
 int pf_device_status(pf_ctx *ctx, unsigned *err_word);

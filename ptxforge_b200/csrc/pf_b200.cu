@@ -446,7 +446,7 @@ int pf_bind(pf_ctx *c, const void *A, const void *B, const float *bias, void *C,
 int pf_launch(pf_ctx *c, void *stream) {
   if (!c) return PF_EINVAL;
   DeviceGuard g(c->device);
-  return do_launch(c, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+  return do_launch(c, static_cast<cudaStream_t>(stream));
 }
 
 int pf_time(pf_ctx *c, int warmup, int iters, int reps, double *median_ms) {
@@ -501,7 +501,7 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
 int pf_device_status(pf_ctx *c, unsigned *err_word) {
   if (!c || !err_word) return PF_EINVAL;
   DeviceGuard g(c->device);
-  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  PF_CUDA(c, cudaDeviceSynchronize());  // launches may be on any stream of this device
   PF_CUDA(c, cudaMemcpy(err_word, c->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost));
   PF_CUDA(c, cudaMemset(c->d_status, 0, sizeof(unsigned)));
   return PF_OK;
