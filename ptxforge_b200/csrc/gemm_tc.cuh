@@ -101,6 +101,62 @@ enum : unsigned {
   kErrTeardownWait = 8u,
 };
 
+// One epilogue warp turns its 32 accumulator rows x BN columns (TMEM lanes q*32.., columns from
+// `t_row`) into C rows [m0, m0+32) x columns [n_tile, n_tile+BN): x*scale + bias[c], GELU, bf16,
+// staged through a double-buffered 32 x 64 swizzled shared-memory box and TMA-stored.
+// `release()` is called by the whole warp right after the last TMEM load of the tile.
+template <int BN, class Release>
+__device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile, const TcParams &p,
+                                              const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
+                                              Release release) {
+  constexpr int EPI_COLS = 64;
+  constexpr int BUF_BYTES = 32 * EPI_COLS * 2;
+#pragma unroll 1
+  for (int c = 0; c < BN / EPI_COLS; ++c) {
+    const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 128;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_row + c * EPI_COLS + h * 32, v);
+      tmem_ld_wait();
+      const int n0 = n_tile + c * EPI_COLS + h * 32;
+      uint32_t packed[16];
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
+        const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
+        const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
+        const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
+        const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
+        packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
+        packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
+      }
+      // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t chunk = static_cast<uint32_t>((h * 4 + i) ^ (lane & 7));
+        st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2], packed[i * 4 + 3]);
+      }
+    }
+    if (c == BN / EPI_COLS - 1) {
+      // Last TMEM read of this accumulator: hand it back to the MMA issuer.
+      tc_fence_before();
+      __syncwarp();
+      release();
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n_tile + c * EPI_COLS, m0);
+      tma_store_commit();
+      tma_store_wait_read<1>();  // the other buffer is free again
+    }
+    __syncwarp();
+    buf ^= 1;
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_bias_gelu_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -268,53 +324,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       }
       tc_fence_after();
       const int m0 = mb * Cfg::BM + q * 32;
-      const int n_tile = nb * Cfg::BN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
-#pragma unroll 1
-      for (int c = 0; c < Cfg::BN / Cfg::EPI_COLS; ++c) {
-        const uint32_t sbuf = smem_u32(ebuf + buf * Cfg::EPI_BUF_BYTES) + lane * 128;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS + h * 32, v);
-          tmem_ld_wait();
-          const int n0 = n_tile + c * Cfg::EPI_COLS + h * 32;
-          uint32_t packed[16];
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
-            const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
-            const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
-            const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
-            const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
-            packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
-            packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
-          }
-          // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t chunk = static_cast<uint32_t>((h * 4 + i) ^ (lane & 7));
-            st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2],
-                         packed[i * 4 + 3]);
-          }
-        }
-        if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
-          // Last TMEM read of this accumulator: hand it back to the MMA warp.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, ebuf + buf * Cfg::EPI_BUF_BYTES, n_tile + c * Cfg::EPI_COLS, m0);
-          tma_store_commit();
-          tma_store_wait_read<1>();  // the other buffer is free again
-        }
-        __syncwarp();
-        buf ^= 1;
-      }
+      uint64_t *tempty_acc = &tempty[acc];
+      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, ebuf, buf, lane, [&] {
+        if (lane == 0) mbar_arrive(tempty_acc);
+      });
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;

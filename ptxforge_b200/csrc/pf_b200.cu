@@ -20,6 +20,7 @@
 #include "pf_b200.h"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 
 #ifndef PF_VERSION_STR
 #define PF_VERSION_STR "0.1.0"
@@ -44,6 +45,8 @@ struct Variant {
   int smem = 0;                // dynamic shared memory
   // tensor path
   int bm = 0, bn = 0, bk_elems = 0, stages = 0, elem = 0;
+  int a_box_rows = 0;           // rows of A per TMA box (the CTA's share of BM)
+  int cta_per_tile = 1;         // 2 = CTA-pair (cluster) kernel
   int b_chunk_n = 0;
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                     const TcParams &) = nullptr;
@@ -74,7 +77,36 @@ Variant make_tc_variant() {
   v.stages = Cfg::STAGES;
   v.elem = Cfg::ELEM;
   v.b_chunk_n = Cfg::B_CHUNK_N;
+  v.a_box_rows = Cfg::BM;
+  v.cta_per_tile = 1;
   v.launch_tc = &launch_tc_impl<DT, BN, ST>;
+  return v;
+}
+
+template <int DT, int ST>
+void launch_tc2_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                     const TcParams &p) {
+  using Cfg = pf::Tc2Config<DT, ST>;
+  pf::gemm_bias_gelu_tc2<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+}
+
+template <int DT, int ST>
+Variant make_tc2_variant() {
+  using Cfg = pf::Tc2Config<DT, ST>;
+  Variant v;
+  v.path = Path::kTensor;
+  v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc2<Cfg>);
+  v.threads = Cfg::THREADS;
+  v.smem = Cfg::SMEM_BYTES;
+  v.bm = Cfg::BM;
+  v.bn = Cfg::BN;
+  v.bk_elems = Cfg::BK;
+  v.stages = Cfg::STAGES;
+  v.elem = Cfg::ELEM;
+  v.b_chunk_n = Cfg::B_CHUNK_N;
+  v.a_box_rows = Cfg::BM_CTA;
+  v.cta_per_tile = 2;
+  v.launch_tc = &launch_tc2_impl<DT, ST>;
   return v;
 }
 
@@ -125,22 +157,30 @@ bool same_tile(const pf_tile &a, const pf_tile &b) {
   return a.BM == b.BM && a.BN == b.BN && a.BK == b.BK && a.TM == b.TM && a.TN == b.TN && a.PAD == b.PAD;
 }
 
-// Tensor-path variant for (dtype, BN, stages).
-bool find_tc_variant(pf_dtype dt, int bn, int stages, Variant *out) {
-  if (dt == PF_BF16) {
-    if (bn == 256 && stages == 4) { *out = make_tc_variant<0, 256, 4>(); return true; }
-    if (bn == 256 && stages == 2) { *out = make_tc_variant<0, 256, 2>(); return true; }
-    if (bn == 128 && stages == 4) { *out = make_tc_variant<0, 128, 4>(); return true; }
-    if (bn == 128 && stages == 2) { *out = make_tc_variant<0, 128, 2>(); return true; }
-    if (bn == 64 && stages == 8) { *out = make_tc_variant<0, 64, 8>(); return true; }
-    if (bn == 64 && stages == 4) { *out = make_tc_variant<0, 64, 4>(); return true; }
-  } else if (dt == PF_E4M3) {
-    if (bn == 256 && stages == 4) { *out = make_tc_variant<1, 256, 4>(); return true; }
-    if (bn == 256 && stages == 2) { *out = make_tc_variant<1, 256, 2>(); return true; }
-    if (bn == 128 && stages == 4) { *out = make_tc_variant<1, 128, 4>(); return true; }
-    if (bn == 128 && stages == 2) { *out = make_tc_variant<1, 128, 2>(); return true; }
-  }
-  return false;
+// Tensor-path variant for (dtype, BM, BN, requested pipeline depth TM).  The depth is clamped to the
+// deepest compiled variant that fits in shared memory (TM=8 asks for "as deep as fits").
+bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, Variant *out) {
+  struct Entry {
+    int dt, bm, bn, stages;
+    Variant (*make)();
+  };
+  static const Entry table[] = {
+      {PF_BF16, 128, 256, 2, &make_tc_variant<0, 256, 2>},  {PF_BF16, 128, 256, 4, &make_tc_variant<0, 256, 4>},
+      {PF_BF16, 128, 128, 2, &make_tc_variant<0, 128, 2>},  {PF_BF16, 128, 128, 4, &make_tc_variant<0, 128, 4>},
+      {PF_BF16, 128, 128, 6, &make_tc_variant<0, 128, 6>},  {PF_BF16, 128, 64, 4, &make_tc_variant<0, 64, 4>},
+      {PF_BF16, 128, 64, 8, &make_tc_variant<0, 64, 8>},    {PF_BF16, 256, 256, 2, &make_tc2_variant<0, 2>},
+      {PF_BF16, 256, 256, 4, &make_tc2_variant<0, 4>},      {PF_BF16, 256, 256, 6, &make_tc2_variant<0, 6>},
+      {PF_E4M3, 128, 256, 2, &make_tc_variant<1, 256, 2>},  {PF_E4M3, 128, 256, 4, &make_tc_variant<1, 256, 4>},
+      {PF_E4M3, 128, 128, 2, &make_tc_variant<1, 128, 2>},  {PF_E4M3, 128, 128, 4, &make_tc_variant<1, 128, 4>},
+      {PF_E4M3, 128, 128, 6, &make_tc_variant<1, 128, 6>},  {PF_E4M3, 256, 256, 2, &make_tc2_variant<1, 2>},
+      {PF_E4M3, 256, 256, 4, &make_tc2_variant<1, 4>},      {PF_E4M3, 256, 256, 6, &make_tc2_variant<1, 6>},
+  };
+  const Entry *best = nullptr;
+  for (const Entry &e : table)
+    if (e.dt == dt && e.bm == bm && e.bn == bn && e.stages <= depth && (!best || e.stages > best->stages)) best = &e;
+  if (!best) return false;
+  *out = best->make();
+  return true;
 }
 
 EncodeTiledFn get_encode_fn() {
@@ -174,6 +214,7 @@ struct pf_ctx {
   int M = 0, N = 0, K = 0;
   Variant var;
   int group_m = 16;
+  int max_units = 0;  // persistent grid: co-resident CTAs (1-CTA) or CTA pairs (2-CTA)
 
   const void *A = nullptr, *B = nullptr;
   const float *bias = nullptr;
@@ -244,7 +285,7 @@ int encode_maps(pf_ctx *c) {
   const uint64_t e = static_cast<uint64_t>(v.elem);
   int rc;
   // A: [M x K], K contiguous; box = BK elements (128 B) x BM rows.
-  rc = encode_2d(c, &c->tmA, in_t, c->A, c->K, c->M, c->K * e, v.bk_elems, v.bm, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_2d(c, &c->tmA, in_t, c->A, c->K, c->M, c->K * e, v.bk_elems, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   // B: [K x N], N contiguous; box = 128 B of N x BK rows.
   rc = encode_2d(c, &c->tmB, in_t, c->B, c->N, c->K, c->N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -275,7 +316,7 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
-    dim3 grid(std::min(p.num_tiles, c->num_sms));
+    dim3 grid(std::min(p.num_tiles, c->max_units) * v.cta_per_tile);
     v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, p);
   } else {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (c->M + v.sbm - 1) / v.sbm);
@@ -384,14 +425,15 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
       return set_err(c, PF_ETILE, "fp32 tile %dx%dx%d t%dx%d p%d is not compiled into this library", t->BM, t->BN,
                      t->BK, t->TM, t->TN, t->PAD);
   } else if (dt == PF_BF16 || dt == PF_E4M3) {
-    if (t->BM != 128) return set_err(c, PF_ETILE, "tensor path: BM must be 128 (one CTA, UMMA M=128), got %d", t->BM);
+    if (t->BM != 128 && t->BM != 256)
+      return set_err(c, PF_ETILE, "tensor path: BM must be 128 (one CTA) or 256 (CTA pair), got %d", t->BM);
     if (t->BK != 32)
       return set_err(c, PF_ETILE, "tensor path: BK must be 32 words (one 128-byte swizzle row), got %d", t->BK);
     if (t->PAD != 0) return set_err(c, PF_ETILE, "tensor path: PAD must be 0, got %d", t->PAD);
     if (t->TN < 1 || t->TN > 64) return set_err(c, PF_ETILE, "tensor path: TN (raster group) out of range: %d", t->TN);
-    if (!find_tc_variant(dt, t->BN, t->TM, &v))
-      return set_err(c, PF_ETILE, "tensor path: no %s kernel with BN=%d and %d stages", dt == PF_BF16 ? "bf16" : "e4m3",
-                     t->BN, t->TM);
+    if (!find_tc_variant(dt, t->BM, t->BN, t->TM, &v))
+      return set_err(c, PF_ETILE, "tensor path: no %s kernel with BM=%d, BN=%d and at most %d stages",
+                     dt == PF_BF16 ? "bf16" : "e4m3", t->BM, t->BN, t->TM);
     const int e = (int)pf_elem_bytes(dt);
     if ((static_cast<long long>(K) * e) % 16 != 0)
       return set_err(c, PF_ESHAPE, "tensor path: rows of A must be a multiple of 16 bytes (K=%d)", K);
@@ -404,6 +446,28 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
   if (v.path == Path::kTensor) {
     cudaError_t e = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
     if (e != cudaSuccess) return set_err(c, PF_ECUDA, "cudaFuncSetAttribute -> %s", cudaGetErrorString(e));
+    // Persistent grid: as many CTAs (or CTA pairs) as can be resident at once.
+    c->max_units = c->num_sms;
+    if (v.cta_per_tile == 2) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (c->num_sms / 2));
+      cfg.blockDim = dim3(v.threads);
+      cfg.dynamicSmemBytes = v.smem;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, v.func, &cfg);
+      if (e != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = c->num_sms / 2;
+      }
+      c->max_units = clusters;
+    }
   }
   c->var = v;
   c->dtype = dt;
@@ -482,7 +546,10 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
   cudaFuncAttributes fa;
   PF_CUDA(c, cudaFuncGetAttributes(&fa, c->var.func));
   int bps = 0;
-  PF_CUDA(c, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, c->var.func, c->var.threads, c->var.smem));
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, c->var.func, c->var.threads, c->var.smem) != cudaSuccess) {
+    cudaGetLastError();  // cluster kernels: the per-SM query may be refused; one CTA per SM by construction
+    bps = 1;
+  }
   out->regs = fa.numRegs;
   out->local_bytes = static_cast<int>(fa.localSizeBytes);
   out->smem_bytes = static_cast<int>(fa.sharedSizeBytes) + c->var.smem;
@@ -491,7 +558,7 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
   out->num_sms = c->num_sms;
   if (c->var.path == Path::kTensor) {
     const int tiles = ((c->M + c->var.bm - 1) / c->var.bm) * ((c->N + c->var.bn - 1) / c->var.bn);
-    out->grid = std::min(tiles, c->num_sms);
+    out->grid = std::min(tiles, c->max_units) * c->var.cta_per_tile;
   } else {
     out->grid = ((c->N + c->var.sbn - 1) / c->var.sbn) * ((c->M + c->var.sbm - 1) / c->var.sbm);
   }

@@ -139,9 +139,10 @@ def test_fp32_cfg2_gate_and_torch(ctx, oracle_mod):
 # bf16 / e4m3 tensor-core path
 # ---------------------------------------------------------------------------------------------
 BF16_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
-              (128, 128, 32, 2, 8, 0), (128, 64, 32, 8, 16, 0), (128, 64, 32, 4, 2, 0)]
+              (128, 128, 32, 8, 8, 0), (128, 64, 32, 8, 16, 0), (128, 64, 32, 4, 2, 0),
+              (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0), (256, 256, 32, 2, 8, 0)]
 E4M3_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
-              (128, 128, 32, 2, 4, 0)]
+              (128, 128, 32, 8, 4, 0), (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0)]
 
 
 @pytest.mark.parametrize("tile", BF16_TILES)
