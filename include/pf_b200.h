@@ -133,6 +133,15 @@ const char *pf_last_error(const pf_ctx *ctx);
 int pf_run_host(pf_ctx *ctx, const void *hA, const void *hB, const float *hbias, void *hC,
                 float scale_a, float scale_b);
 
+/* The two halves of pf_run_host for callers that launch and time in between: pf_upload copies host
+ * operands into context-owned device buffers (allocated on first use, re-used while the problem
+ * size is unchanged), binds them and synchronises -- CudaRunner::Impl::ensure
+ * (cuda_runner.cpp:91-108).  pf_download copies the context-owned C back after synchronising the
+ * device -- the gate's cuMemcpyDtoH (cuda_runner.cpp:188). */
+int pf_upload(pf_ctx *ctx, const void *hA, const void *hB, const float *hbias, float scale_a,
+              float scale_b);
+int pf_download(pf_ctx *ctx, void *hC);
+
 /* ---- row sharding (no collective on the hot path) ----------------------------------------- */
 
 /* Rows [*row0, *row0 + *rows) of A and C that shard `g` of `G` owns for an M-row problem.  Shard

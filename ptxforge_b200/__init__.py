@@ -29,7 +29,7 @@ OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
 # Exported symbols (every entry point of include/pf_b200.h).
 SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
-           "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout")
+           "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download")
 
 
 class Tile(ctypes.Structure):
@@ -95,6 +95,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_last_error.restype = ctypes.c_char_p
         lib.pf_run_host.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
+        lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
+        lib.pf_download.argtypes = [vp, vp]
         lib.pf_elem_bytes.argtypes = [i]
         lib.pf_elem_bytes.restype = ctypes.c_size_t
         lib.pf_out_bytes.argtypes = [i]
@@ -103,7 +105,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_selftest_wait_timeout.argtypes = [vp, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
-                     "pf_selftest_wait_timeout"):
+                     "pf_selftest_wait_timeout", "pf_upload", "pf_download"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -209,6 +211,14 @@ class Context:
         """H2D copies of host operands, launch, D2H of C, synchronise (pf_run_host)."""
         self._check(self._lib.pf_run_host(self._h, _ptr(hA), _ptr(hB), _ptr(hbias), _ptr(hC), scale_a, scale_b),
                     "pf_run_host")
+
+    def upload(self, hA, hB, hbias, scale_a: float = 1.0, scale_b: float = 1.0):
+        """H2D copies into context-owned device operands and bind them (pf_upload)."""
+        self._check(self._lib.pf_upload(self._h, _ptr(hA), _ptr(hB), _ptr(hbias), scale_a, scale_b), "pf_upload")
+
+    def download(self, hC):
+        """D2H copy of the context-owned C (pf_download)."""
+        self._check(self._lib.pf_download(self._h, _ptr(hC)), "pf_download")
 
     def selftest_wait_timeout(self, ns: int) -> int:
         w = ctypes.c_uint()

@@ -69,5 +69,35 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+REF_ROOT = os.environ.get("PTXFORGE_REFERENCE", "/root/reference")
+TUNE_SRC = os.path.join(HERE, "host", "tune_b200.cpp")
+TUNE_BIN = os.path.join(ROOT, "build", "ptxforge-tune-b200")
+
+
+def tune_command(out: str, lib_dir: str, rpath: str, ref_root: str = REF_ROOT) -> list[str]:
+    """g++ line for PTXForge's tuner CLI with the B200 runner, against the libpf_b200.so in lib_dir."""
+    return ["g++", "-std=c++20", "-O2", "-Wall", "-Wextra", "-I", INCLUDE,
+            "-I", os.path.join(ref_root, "core", "include"), "-I", os.path.join(ref_root, "compiler", "include"),
+            TUNE_SRC, "-L", lib_dir, "-lpf_b200", f"-Wl,-rpath,{rpath}", "-lpthread", "-o", out]
+
+
+def build_tune(force: bool = False, ref_root: str = REF_ROOT) -> str | None:
+    """Build build/ptxforge-tune-b200 when the PTXForge headers are available (they are not shipped here:
+    the runner is compiled inside the PTXForge tree it plugs into)."""
+    if not os.path.isdir(os.path.join(ref_root, "core", "include", "ptxforge")):
+        return None
+    deps = [TUNE_SRC, LIB, os.path.join(INCLUDE, "ptxforge_b200", "b200_runner.hpp"), os.path.join(INCLUDE, "pf_b200.h")]
+    if force or _stale(TUNE_BIN, deps):
+        os.makedirs(os.path.dirname(TUNE_BIN), exist_ok=True)
+        # $ORIGIN-relative rpath: the binary finds the library wherever the repository is copied
+        cmd = tune_command(TUNE_BIN + ".tmp", HERE, "$ORIGIN/../ptxforge_b200", ref_root)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("g++ failed:\n" + (r.stdout + r.stderr)[-6000:])
+        os.replace(TUNE_BIN + ".tmp", TUNE_BIN)
+    return TUNE_BIN
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_tune(force="--force" in sys.argv))

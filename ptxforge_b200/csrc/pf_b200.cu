@@ -574,11 +574,12 @@ int pf_device_status(pf_ctx *c, unsigned *err_word) {
   return PF_OK;
 }
 
-int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, void *hC, float sa, float sb) {
-  if (!c) return PF_EINVAL;
-  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_run_host before pf_prepare");
-  if (!hA || !hB || !hbias || !hC) return set_err(c, PF_EINVAL, "null host operand");
-  DeviceGuard g(c->device);
+}  // extern "C"
+
+namespace {
+// Context-owned device operands sized for the prepared problem; async H2D copies on the context's
+// stream; bind.  Shared by pf_upload and pf_run_host.
+int stage_inputs(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
   const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
   const size_t nA = static_cast<size_t>(c->M) * c->K * e, nB = static_cast<size_t>(c->K) * c->N * e;
   const size_t nC = static_cast<size_t>(c->M) * c->N * o, nBias = static_cast<size_t>(c->N) * sizeof(float);
@@ -606,20 +607,56 @@ int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, v
       c->sa != sa || c->sb != sb) {
     if ((rc = pf_bind(c, c->hbufA, c->hbufB, c->hbufBias, c->hbufC, sa, sb))) return rc;
   }
+  return PF_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, void *hC, float sa, float sb) {
+  if (!c) return PF_EINVAL;
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_run_host before pf_prepare");
+  if (!hA || !hB || !hbias || !hC) return set_err(c, PF_EINVAL, "null host operand");
+  DeviceGuard g(c->device);
+  int rc;
+  if ((rc = stage_inputs(c, hA, hB, hbias, sa, sb))) return rc;
   if ((rc = do_launch(c, c->stream))) return rc;
+  const size_t nC = static_cast<size_t>(c->M) * c->N * pf_out_bytes(c->dtype);
   PF_CUDA(c, cudaMemcpyAsync(hC, c->hbufC, nC, cudaMemcpyDeviceToHost, c->stream));
   PF_CUDA(c, cudaStreamSynchronize(c->stream));
   return PF_OK;
 }
 
+int pf_upload(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
+  if (!c) return PF_EINVAL;
+  if (!c->prepared) return set_err(c, PF_ESTATE, "pf_upload before pf_prepare");
+  if (!hA || !hB || !hbias) return set_err(c, PF_EINVAL, "null host operand");
+  DeviceGuard g(c->device);
+  int rc;
+  if ((rc = stage_inputs(c, hA, hB, hbias, sa, sb))) return rc;
+  PF_CUDA(c, cudaMemsetAsync(c->hbufC, 0, static_cast<size_t>(c->M) * c->N * pf_out_bytes(c->dtype), c->stream));
+  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  return PF_OK;
+}
+
+int pf_download(pf_ctx *c, void *hC) {
+  if (!c || !hC) return PF_EINVAL;
+  if (!c->prepared || !c->hbufC || c->C != c->hbufC)
+    return set_err(c, PF_ESTATE, "pf_download without context-owned operands (call pf_upload first)");
+  DeviceGuard g(c->device);
+  PF_CUDA(c, cudaDeviceSynchronize());
+  const size_t nC = static_cast<size_t>(c->M) * c->N * pf_out_bytes(c->dtype);
+  PF_CUDA(c, cudaMemcpy(hC, c->hbufC, nC, cudaMemcpyDeviceToHost));
+  return PF_OK;
+}
+
 int pf_shard_rows(int M, int G, int g, int align, int *row0, int *rows) {
   if (M <= 0 || G <= 0 || g < 0 || g >= G || align <= 0 || !row0 || !rows) return PF_EINVAL;
-  // Split M into `blocks` units of `align` rows, spread as evenly as possible; the remainder rows of
-  // a ragged M go to the last shard.
-  const long long blocks = M / align;
-  const long long lo = blocks * g / G, hi = blocks * (g + 1) / G;
-  long long r0 = lo * align, r1 = hi * align;
-  if (g == G - 1) r1 = M;
+  // Split M into ceil(M / align) units of `align` rows (the last one partial for a ragged M) and give
+  // shard g units [units*g/G, units*(g+1)/G): shard sizes differ by at most one unit.
+  const long long units = (static_cast<long long>(M) + align - 1) / align;
+  const long long lo = units * g / G, hi = units * (g + 1) / G;
+  const long long r0 = std::min<long long>(lo * align, M), r1 = std::min<long long>(hi * align, M);
   *row0 = static_cast<int>(r0);
   *rows = static_cast<int>(r1 - r0);
   return PF_OK;

@@ -237,8 +237,13 @@ def test_invalid_configs_are_errors(ctx, pf):
         ctx.prepare("bf16", (64, 256, 32, 4, 16, 0), 256, 256, 256)
     assert e.value.code == pf.PF_ETILE
     with pytest.raises(pf.PFError) as e:
-        ctx.prepare("bf16", (128, 256, 32, 16, 16, 0), 256, 256, 256)
+        ctx.prepare("bf16", (128, 256, 16, 4, 16, 0), 256, 256, 256)  # 64-byte k-blocks: not built
     assert e.value.code == pf.PF_ETILE
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare("e4m3", (128, 64, 32, 4, 16, 0), 256, 256, 256)  # e4m3 B rows are 128 wide
+    assert e.value.code == pf.PF_ETILE
+    # TM is a requested pipeline depth, clamped to the deepest compiled variant that fits
+    ctx.prepare("bf16", (128, 256, 32, 16, 16, 0), 256, 256, 256)
     with pytest.raises(pf.PFError) as e:
         ctx.prepare("bf16", None, 256, 100, 256)  # 200-byte rows of B and C: not a TMA row
     assert e.value.code == pf.PF_ESHAPE

@@ -1,0 +1,135 @@
+"""B200Runner and PTXForge's tuner, on a fake libpf_b200 (CPU only).
+
+The C++ runner (include/ptxforge_b200/b200_runner.hpp) and the tuner CLI (ptxforge_b200/host/tune_b200.cpp)
+are compiled against PTXForge's own headers and linked to tests/fake_pf/fake_pf.c, a CPU implementation of
+the C ABI -- the reference's fake-driver pattern (tests/fake_cuda/run.sh) moved to this backend's boundary.
+Checked: the correctness gate, M-row sharding over several devices, the trace contract of tune(), and
+failure handling (refused tiles, wrong results, launch failure, out of memory, a device-side timeout on one
+shard, a device that does not open) -- every failure is a failed trial with a message, never a crash.
+Needs the PTXForge headers at build time (skipped where they are absent).
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from ptxforge_b200 import build as pbuild  # noqa: E402
+
+HAVE_REF = os.path.isdir(os.path.join(pbuild.REF_ROOT, "core", "include", "ptxforge"))
+pytestmark = pytest.mark.skipif(not HAVE_REF, reason="PTXForge headers not available")
+
+
+@pytest.fixture(scope="module")
+def tune_fake(tmp_path_factory):
+    d = tmp_path_factory.mktemp("fake_pf")
+    lib = d / "libpf_b200.so"
+    subprocess.run(["gcc", "-std=c11", "-O1", "-fPIC", "-shared", "-Wall", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "fake_pf", "fake_pf.c"), "-o", str(lib), "-lm"], check=True)
+    exe = d / "ptxforge-tune-b200"
+    r = subprocess.run(pbuild.tune_command(str(exe), str(d), str(d)), capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return str(exe), d
+
+
+def run(tune_fake, args, **env):
+    exe, d = tune_fake
+    e = dict(os.environ)
+    e.update({k: str(v) for k, v in env.items()})
+    return subprocess.run([exe, *args], capture_output=True, text=True, env=e, cwd=str(d), timeout=120)
+
+
+SMALL = ["--M", "256", "--N", "256", "--K", "128"]
+GOOD = ["--BM", "128", "--BN", "256", "--BK", "32", "--TM", "4", "--TN", "16", "--PAD", "0"]
+
+
+def measure(tune_fake, extra, **env):
+    r = run(tune_fake, ["measure", "--dtype", "bf16", *SMALL, *extra], **env)
+    line = r.stdout.strip().splitlines()[-1] if r.stdout.strip() else "{}"
+    return r.returncode, json.loads(line), r
+
+
+def test_measure_ok_and_gated(tune_fake):
+    rc, j, _ = measure(tune_fake, GOOD)
+    assert rc == 0 and j["ok"] and j["gflops"] > 0
+    assert j["profile"]["max_err"] < 2e-2
+    assert j["profile"]["regs"] == 149 and j["cublas_gflops"] is None
+
+
+@pytest.mark.parametrize("gpus", [2, 3, 8])
+def test_measure_sharded_over_gpus(tune_fake, tmp_path, gpus):
+    log = tmp_path / "calls.log"
+    rc, j, _ = measure(tune_fake, GOOD + ["--gpus", str(gpus), "--M", "1000"], FAKE_PF_LOG=log)
+    assert rc == 0 and j["ok"], j
+    lines = log.read_text().split()
+    devices = {int(d) for what, d in zip(lines[::2], lines[1::2]) if what == "launch"}
+    # 1000 rows = 8 units of up to 128 rows: every device got a shard and launched
+    assert devices == set(range(gpus))
+    # the trial's time is the slowest shard's (the fake reports 0.01 ms more per device index)
+    slowest = max(devices)
+    assert abs(j["ms"] - (1.0 + 0.001 * (256 + 8 + 16) + 0.01 * slowest)) < 1e-9
+
+
+def test_fp32_path(tune_fake):
+    r = run(tune_fake, ["measure", "--dtype", "f32", "--M", "128", "--N", "128", "--K", "64", "--BM", "128", "--BN",
+                        "128", "--BK", "8", "--TM", "8", "--TN", "8", "--PAD", "4"])
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and j["ok"] and j["profile"]["max_err"] < 1e-5
+
+
+def test_e4m3_path(tune_fake):
+    r = run(tune_fake, ["measure", "--dtype", "e4m3", *SMALL, *GOOD])
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and j["ok"] and j["profile"]["max_err"] < 5e-2
+
+
+def test_unmappable_config_is_a_failed_trial(tune_fake):
+    rc, j, _ = measure(tune_fake, ["--BM", "64", "--BN", "64", "--BK", "8", "--TM", "4", "--TN", "4", "--PAD", "0"])
+    assert rc == 4 and not j["ok"] and "BM must be" in j["error"]
+
+
+def test_bk_and_pad_are_canonical_on_the_tensor_path(tune_fake):
+    rc, j, _ = measure(tune_fake, ["--BM", "128", "--BN", "128", "--BK", "8", "--TM", "4", "--TN", "8", "--PAD", "2"])
+    assert rc == 0 and j["ok"]
+
+
+@pytest.mark.parametrize("env,needle", [({"FAKE_PF_WRONG": 1}, "incorrect result"),
+                                        ({"FAKE_PF_FAIL_LAUNCH": 1}, "fake launch failure"),
+                                        ({"FAKE_PF_NOMEM": 1}, "cudaMalloc")])
+def test_injected_failures(tune_fake, env, needle):
+    rc, j, _ = measure(tune_fake, GOOD, **env)
+    assert rc == 4 and not j["ok"] and needle in j["error"], j
+
+
+def test_timeout_on_one_shard_names_the_gpu(tune_fake):
+    rc, j, _ = measure(tune_fake, GOOD + ["--gpus", "2"], FAKE_PF_TIMEOUT_DEV=1)
+    assert rc == 4 and j["error"].startswith("gpu 1:") and "bounded device wait" in j["error"]
+
+
+def test_device_that_does_not_open(tune_fake):
+    rc, _, r = measure(tune_fake, GOOD + ["--gpus", "2"], FAKE_PF_FAIL_OPEN=1)
+    assert rc == 1 and "pf_open(device 1)" in r.stderr
+
+
+def test_tune_trace_contract(tune_fake, tmp_path):
+    out = tmp_path / "trace.json"
+    r = run(tune_fake, ["tune", "--dtype", "bf16", *SMALL, "--budget", "10", "--advisor", "rules", "--gpus", "2",
+                        "--out", str(out)])
+    assert r.returncode == 0, r.stderr
+    t = json.loads(out.read_text())
+    assert t["schema"] == 1 and t["source"] == "harness" and t["warning"] is None
+    assert t["gpu"]["arch"] == "sm_100a" and t["gpu"]["sms"] == 148
+    assert len(t["trials"]) == 10
+    cfgs = [json.dumps(x["cfg"], sort_keys=True) for x in t["trials"]]
+    assert len(set(cfgs)) == len(cfgs)  # no duplicate trials
+    for tr in t["trials"]:
+        assert tr["ok"] or tr["error"]
+    assert any(tr["ok"] for tr in t["trials"])
+    assert t["best_gflops"] is not None
+    names = [s["name"] for s in t["stages"]]
+    assert names == ["CUDA C++ source", "LLVM IR", "PTX"]
+    assert ".entry" not in t["stages"][2]["text"]  # no compiler-written PTX embedded
