@@ -134,7 +134,16 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------
-# distributed plumbing (one process per GPU; no collective on the data path)
+# distributed plumbing (one process per GPU; no collective on the data path): ptxforge_b200.dist
+# ------------------------------------------------------------------------------------------------
+def Dist(n_gpus: int):
+    from ptxforge_b200.dist import Ranks
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    return Ranks("nccl")
+
+
 # ------------------------------------------------------------------------------------------------
 class Dist:
     def __init__(self, n_gpus: int):
