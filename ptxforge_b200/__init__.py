@@ -29,7 +29,8 @@ OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
 # Exported symbols (every entry point of include/pf_b200.h).
 SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
-           "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download")
+           "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
+           "pf_gemm_bias_gelu_noalloc")
 
 
 class Tile(ctypes.Structure):
@@ -97,6 +98,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
         lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_download.argtypes = [vp, vp]
+        lib.pf_gemm_bias_gelu_noalloc.argtypes = [i, i, ctypes.POINTER(Tile), i, i, i, vp, vp, vp, vp, ctypes.c_float,
+                                                  ctypes.c_float, vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p,
+                                                  ctypes.c_size_t]
         lib.pf_elem_bytes.argtypes = [i]
         lib.pf_elem_bytes.restype = ctypes.c_size_t
         lib.pf_out_bytes.argtypes = [i]
@@ -105,7 +109,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_selftest_wait_timeout.argtypes = [vp, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
-                     "pf_selftest_wait_timeout", "pf_upload", "pf_download"):
+                     "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -224,6 +228,25 @@ class Context:
         w = ctypes.c_uint()
         self._check(self._lib.pf_selftest_wait_timeout(self._h, ns, ctypes.byref(w)), "pf_selftest_wait_timeout")
         return w.value
+
+
+def gemm_bias_gelu_noalloc(device: int, dtype: str, tile, M: int, N: int, K: int, A, B, bias, C,
+                           scale_a: float = 1.0, scale_b: float = 1.0, stream=None, sync: bool = True) -> int:
+    """pf_gemm_bias_gelu_noalloc: the bf16 / e4m3 kernel on caller-owned device operands, for callers
+    that cannot allocate GPU memory at call time (no context, no cudaMalloc; the kernel's scratch is a
+    fixed array inside the library).  With sync=True waits for the kernel and returns its status word
+    (raising PFError if a bounded device wait ran out); with sync=False returns 0 after queueing."""
+    lib = load_library()
+    t = tile if isinstance(tile, Tile) else Tile(*(tile or DEFAULT_TILES[dtype]))
+    s = 0 if stream is None else (stream if isinstance(stream, int) else int(stream.cuda_stream))
+    st = ctypes.c_uint(0)
+    err = ctypes.create_string_buffer(256)
+    rc = lib.pf_gemm_bias_gelu_noalloc(device, DTYPES[dtype], ctypes.byref(t), M, N, K, _ptr(A), _ptr(B),
+                                       _ptr(bias), _ptr(C), scale_a, scale_b, s,
+                                       ctypes.byref(st) if sync else None, err, len(err))
+    if rc:
+        raise PFError(rc, "pf_gemm_bias_gelu_noalloc: " + err.value.decode())
+    return st.value
 
 
 _contexts: dict = {}

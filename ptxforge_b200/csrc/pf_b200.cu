@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -692,4 +693,153 @@ extern "C" int pf_selftest_wait_timeout(pf_ctx *c, unsigned long long timeout_ns
   selftest_wait_kernel<<<1, 32, 0, c->stream>>>(c->d_status, timeout_ns);
   PF_CUDA(c, cudaGetLastError());
   return pf_device_status(c, err_word);
+}
+
+// ------------------------------------------------------------------------------------------------
+// No-allocation entry point (no counterpart in the reference).  For callers that cannot allocate
+// GPU memory at call time: the tensor-core kernel's scratch (its device status word) lives in this
+// fixed, file-scope array instead of a cudaMalloc'ed word of a pf_ctx.  Every GPU that loads the
+// library holds the array until the process exits.
+// ------------------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char pf_noalloc_scratch[PF_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+
+// Per-device set-up, done once with that device current: the array's device address (host code
+// cannot use the symbol itself -- on the host it names a stand-in, not device memory).
+struct NoallocDevice {
+  std::once_flag once;
+  cudaError_t setup_err = cudaSuccess;
+  unsigned *scratch = nullptr;
+  int num_sms = 0;
+  int cc_major = 0;
+};
+NoallocDevice g_noalloc_dev[kNoallocMaxDevices];
+
+int noalloc_fail(char *err, size_t len, int code, const char *fmt, ...) {
+  if (err && len) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, len, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+}  // namespace
+
+extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_tile *t, int M, int N, int K,
+                                         const void *A, const void *B, const float *bias, void *C, float sa,
+                                         float sb, void *stream, unsigned *status_out, char *err,
+                                         size_t err_len) {
+  if (err && err_len) err[0] = '\0';
+  if (!t || !A || !B || !bias || !C) return noalloc_fail(err, err_len, PF_EINVAL, "null argument");
+  if (M <= 0 || N <= 0 || K <= 0)
+    return noalloc_fail(err, err_len, PF_EINVAL, "M, N, K must be positive (got %d, %d, %d)", M, N, K);
+  if (dtype != PF_BF16 && dtype != PF_E4M3)
+    return noalloc_fail(err, err_len, PF_EINVAL, "only the bf16 / e4m3 tensor-core kernels run without allocation");
+  if (dtype == PF_BF16 && (sa != 1.f || sb != 1.f))
+    return noalloc_fail(err, err_len, PF_EINVAL, "scales apply to e4m3 operands only");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= kNoallocMaxDevices) {
+    cudaGetLastError();
+    return noalloc_fail(err, err_len, PF_ENODEV, "no CUDA device %d", device);
+  }
+  DeviceGuard g(device);
+  NoallocDevice &d = g_noalloc_dev[device];
+  std::call_once(d.once, [&] {
+    void *p = nullptr;
+    d.setup_err = cudaGetSymbolAddress(&p, pf_noalloc_scratch);
+    if (d.setup_err == cudaSuccess)
+      d.setup_err = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (d.setup_err == cudaSuccess)
+      d.setup_err = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, device);
+    d.scratch = static_cast<unsigned *>(p);
+  });
+  if (d.setup_err != cudaSuccess || !d.scratch)
+    return noalloc_fail(err, err_len, PF_ECUDA, "scratch set-up on device %d failed: %s", device,
+                        cudaGetErrorString(d.setup_err));
+  if (d.cc_major != 10) return noalloc_fail(err, err_len, PF_ENODEV, "device %d is not an sm_100 GPU", device);
+
+  // Kernel variant and layout rules: those of pf_prepare / pf_bind.
+  if ((t->BM != 128 && t->BM != 256) || t->BK != 32 || t->PAD != 0 || t->TN < 1 || t->TN > 64)
+    return noalloc_fail(err, err_len, PF_ETILE, "tile %dx%dx%d t%dx%d p%d has no tensor-core kernel", t->BM, t->BN,
+                        t->BK, t->TM, t->TN, t->PAD);
+  Variant v;
+  if (!find_tc_variant(dtype, t->BM, t->BN, t->TM, &v))
+    return noalloc_fail(err, err_len, PF_ETILE, "no kernel with BM=%d, BN=%d and at most %d stages", t->BM, t->BN,
+                        t->TM);
+  const long long e = static_cast<long long>(pf_elem_bytes(dtype));
+  if ((K * e) % 16 != 0 || (N * e) % 16 != 0 || (N * 2LL) % 16 != 0)
+    return noalloc_fail(err, err_len, PF_ESHAPE, "rows of A, B and C must be multiples of 16 bytes (N=%d, K=%d)", N, K);
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(bias))
+    return noalloc_fail(err, err_len, PF_EINVAL, "operands must be 16-byte aligned");
+  // Scratch this kernel needs: one 32-bit status word.
+  constexpr size_t kScratchNeeded = sizeof(unsigned);
+  if (kScratchNeeded > sizeof(pf_noalloc_scratch))
+    return noalloc_fail(err, err_len, PF_EINVAL, "the kernel needs %zu bytes of scratch; the fixed area holds %zu",
+                        kScratchNeeded, sizeof(pf_noalloc_scratch));
+
+  cudaError_t ce = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
+  if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce));
+  int units = d.num_sms;
+  if (v.cta_per_tile == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (d.num_sms / 2));
+    cfg.blockDim = dim3(v.threads);
+    cfg.dynamicSmemBytes = v.smem;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, v.func, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = d.num_sms / 2;
+    }
+    units = clusters;
+  }
+
+  const CUtensorMapDataType in_t =
+      dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap tmA, tmB, tmC;
+  if (encode_2d(nullptr, &tmA, in_t, A, K, M, K * e, v.bk_elems, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      encode_2d(nullptr, &tmB, in_t, B, N, K, N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      encode_2d(nullptr, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");
+
+  TcParams p;
+  p.bias = bias;
+  p.scale = sa * sb;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blocks = (M + v.bm - 1) / v.bm;
+  p.num_n_blocks = (N + v.bn - 1) / v.bn;
+  p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+  p.k_blocks = (K + v.bk_elems - 1) / v.bk_elems;
+  p.group_m = std::max(1, std::min(t->TN, p.num_m_blocks));
+  p.status = d.scratch;  // word 0 of the fixed scratch area
+  p.timeout_ns = 4000000000ull;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ce = cudaMemsetAsync(d.scratch, 0, sizeof(unsigned), s);  // the last call's status must not leak in
+  if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
+  v.launch_tc(dim3(std::min(p.num_tiles, units) * v.cta_per_tile), s, tmA, tmB, tmC, p);
+  ce = cudaGetLastError();
+  if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "launch: %s", cudaGetErrorString(ce));
+  if (status_out) {
+    unsigned w = 0;
+    ce = cudaMemcpyAsync(&w, d.scratch, sizeof w, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "status read: %s", cudaGetErrorString(ce));
+    *status_out = w;
+    if (w) return noalloc_fail(err, err_len, PF_ETIMEOUT, "a bounded device wait ran out (status 0x%x)", w);
+  }
+  return PF_OK;
 }
