@@ -55,10 +55,12 @@ typedef enum {
 
 /* The tuner's tile config: exactly the fields of ptxforge::Config (core/include/ptxforge/space.hpp:58).
  *   fp32 path   : the reference meaning (block tile BM x BN, K step BK, TM x TN per thread, PAD).
- *   tensor path : BM = CTA rows (128), BN = UMMA N (64/128/256), BK = K-block in 4-byte words
- *                 (32 = one 128-byte swizzle row), TM = smem pipeline stages, TN = tile-raster group
- *                 height in M blocks (consecutive tiles walk TN row blocks before moving along N),
- *                 PAD = 0. */
+ *   tensor path : BM = tile rows: 128 (one CTA, UMMA M=128) or 256 (a CTA pair, cta_group::2);
+ *                 BN = UMMA N (64/128/256; 256 for BM=256); BK = 32 (4-byte words of one 128-byte
+ *                 swizzle row); TM = requested pipeline depth in stages (clamped to the deepest
+ *                 compiled variant that fits shared memory); TN = tile-raster group height in M
+ *                 blocks (consecutive tiles walk TN row blocks before moving along N); PAD = extra
+ *                 128-byte k-atoms per stage (0: one atom = 64 bf16 / 128 e4m3 k, 1: two atoms). */
 typedef struct {
   int BM, BN, BK, TM, TN, PAD;
 } pf_tile;

@@ -87,15 +87,16 @@ class B200Runner : public Runner {
 
   std::string source() const override { return "harness"; }
 
-  // The tuner's Config onto a pf_tile.  On the tensor-core path BK and PAD have no counterpart (the
-  // k-block is one 128-byte swizzle row; TMA swizzling replaces shared-memory padding): they are set to
-  // 32 and 0, so every (BM, BN, TM, TN) the search proposes reaches a kernel when one exists.  BM, BN,
-  // TM and TN keep the meaning pf_b200.h gives them.  The fp32 path takes the Config as it is.
+  // The tuner's Config onto a pf_tile.  On the tensor-core path the k-block is made of 128-byte swizzle
+  // atoms, so BK has no counterpart and is set to 32, and PAD (shared-memory padding in the SIMT kernel)
+  // selects one (PAD=0) or two (PAD>=1) k-atoms per stage; every (BM, BN, TM, TN) the search proposes
+  // then reaches a kernel when one exists.  BM, BN, TM and TN keep the meaning pf_b200.h gives them.
+  // The fp32 path takes the Config as it is.
   pf_tile to_tile(const Config &c) const {
     pf_tile t{c.BM, c.BN, c.BK, c.TM, c.TN, c.PAD};
     if (opt_.dtype == PF_BF16 || opt_.dtype == PF_E4M3) {
       t.BK = 32;
-      t.PAD = 0;
+      t.PAD = c.PAD >= 1 ? 1 : 0;
     }
     return t;
   }

@@ -52,12 +52,13 @@ class Attr(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
-# Best-measured defaults per dtype (tensor path: BM=128, BN=256, BK=32 words, 4 stages,
-# raster group 16 M-blocks; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4).
+# Best-measured defaults per dtype.  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
+# stage (PAD=1) and as many stages as fit (TM=8 -> 3), raster group 8 M-blocks (TN=8) -- the lowest energy
+# per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4.
 DEFAULT_TILES = {
     "f32": (128, 128, 8, 8, 8, 4),
-    "bf16": (128, 256, 32, 4, 16, 0),
-    "e4m3": (128, 256, 32, 4, 16, 0),
+    "bf16": (256, 256, 32, 8, 8, 1),
+    "e4m3": (256, 256, 32, 8, 8, 1),
 }
 
 

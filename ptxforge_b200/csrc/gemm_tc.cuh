@@ -41,15 +41,18 @@ struct TcParams {
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).
-template <int kDtype, int kBN, int kStages>
+template <int kDtype, int kBN, int kStages, int kKAtoms = 1>
 struct TcConfig {
   static constexpr int BM = 128;
   static constexpr int BN = kBN;
   static constexpr int STAGES = kStages;
   static constexpr int ELEM = (kDtype == 0) ? 2 : 1;        // bytes per A/B element
-  static constexpr int BK = 128 / ELEM;                      // k elements per stage = one 128-B row
+  static constexpr int KATOMS = kKAtoms;                     // 128-byte k-atoms per stage
+  static constexpr int ATOM_K = 128 / ELEM;                  // k elements in one 128-B swizzle row
+  static constexpr int BK = KATOMS * ATOM_K;                 // k elements per stage
   static constexpr int UMMA_K = 32 / ELEM;                   // k per tcgen05.mma
-  static constexpr int A_BYTES = BM * 128;                   // 128 rows x 128 B
+  static constexpr int A_ATOM_BYTES = BM * 128;              // 128 rows x 128 B
+  static constexpr int A_BYTES = KATOMS * A_ATOM_BYTES;
   static constexpr int B_CHUNK_N = 128 / ELEM;               // N elements per 128-B row of B
   static constexpr int B_CHUNKS = BN / B_CHUNK_N;            // TMA boxes of B per stage
   static constexpr int B_CHUNK_BYTES = BK * 128;             // BK rows x 128 B
@@ -228,7 +231,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
+#pragma unroll
+          for (int a = 0; a < Cfg::KATOMS; ++a)
+            tma_load_2d(sA + stage * Cfg::A_BYTES + a * Cfg::A_ATOM_BYTES, &tmA, &full[stage],
+                        kb * Cfg::BK + a * Cfg::ATOM_K, mb * Cfg::BM);
           uint8_t *b_dst = sB + stage * Cfg::B_BYTES;
 #pragma unroll
           for (int j = 0; j < Cfg::B_CHUNKS; ++j)
@@ -278,8 +284,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-            // A: K-major, 128-B swizzle; k advances 32 bytes inside the swizzle row.
-            const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+            // A: K-major, 128-B swizzle; k advances 32 bytes inside a swizzle row, then to the next atom.
+            constexpr int PER_ATOM = Cfg::ATOM_K / Cfg::UMMA_K;
+            const uint64_t ad =
+                smem_desc(a_addr + (k / PER_ATOM) * Cfg::A_ATOM_BYTES + (k % PER_ATOM) * 32, 16, 1024, kSwizzle128B);
             // B: N-major, 128-B swizzle; k advances UMMA_K rows of 128 B; LBO = next 128-B column chunk.
             const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
             if constexpr (Cfg::ELEM == 2)

@@ -18,7 +18,7 @@
 
 namespace pf {
 
-template <int kDtype, int kStages>
+template <int kDtype, int kStages, int kKAtoms = 1>
 struct Tc2Config {
   static constexpr int BM = 256;                             // pair tile rows
   static constexpr int BM_CTA = 128;
@@ -26,9 +26,12 @@ struct Tc2Config {
   static constexpr int BN_CTA = 128;                         // B columns loaded by each CTA
   static constexpr int STAGES = kStages;
   static constexpr int ELEM = (kDtype == 0) ? 2 : 1;
-  static constexpr int BK = 128 / ELEM;
+  static constexpr int KATOMS = kKAtoms;                     // 128-byte k-atoms per stage
+  static constexpr int ATOM_K = 128 / ELEM;
+  static constexpr int BK = KATOMS * ATOM_K;
   static constexpr int UMMA_K = 32 / ELEM;
-  static constexpr int A_BYTES = BM_CTA * 128;
+  static constexpr int A_ATOM_BYTES = BM_CTA * 128;
+  static constexpr int A_BYTES = KATOMS * A_ATOM_BYTES;
   static constexpr int B_CHUNK_N = 128 / ELEM;
   static constexpr int B_CHUNKS = BN_CTA / B_CHUNK_N;
   static constexpr int B_CHUNK_BYTES = BK * 128;
@@ -125,7 +128,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
           const uint32_t bar = pair_leader_addr(smem_u32(&full[stage]));
-          tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * Cfg::BK, m0);
+#pragma unroll
+          for (int a = 0; a < Cfg::KATOMS; ++a)
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES + a * Cfg::A_ATOM_BYTES, &tmA, bar,
+                             kb * Cfg::BK + a * Cfg::ATOM_K, m0);
           uint8_t *b_dst = sB + stage * Cfg::B_BYTES;
 #pragma unroll
           for (int j = 0; j < Cfg::B_CHUNKS; ++j)
@@ -173,7 +179,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-            const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+            constexpr int PER_ATOM = Cfg::ATOM_K / Cfg::UMMA_K;
+            const uint64_t ad =
+                smem_desc(a_addr + (k / PER_ATOM) * Cfg::A_ATOM_BYTES + (k % PER_ATOM) * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
             if constexpr (Cfg::ELEM == 2)
               tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);

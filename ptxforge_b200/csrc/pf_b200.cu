@@ -47,6 +47,8 @@ struct Variant {
   // tensor path
   int bm = 0, bn = 0, bk_elems = 0, stages = 0, elem = 0;
   int a_box_rows = 0;           // rows of A per TMA box (the CTA's share of BM)
+  int a_box_k = 0;              // k elements per TMA box of A (one 128-byte swizzle row)
+  int katoms = 1;               // 128-byte k-atoms per pipeline stage
   int cta_per_tile = 1;         // 2 = CTA-pair (cluster) kernel
   int b_chunk_n = 0;
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
@@ -57,16 +59,16 @@ struct Variant {
                       bool vec) = nullptr;
 };
 
-template <int DT, int BN, int ST>
+template <int DT, int BN, int ST, int KA>
 void launch_tc_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                     const TcParams &p) {
-  using Cfg = TcConfig<DT, BN, ST>;
+  using Cfg = TcConfig<DT, BN, ST, KA>;
   pf::gemm_bias_gelu_tc<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
 }
 
-template <int DT, int BN, int ST>
+template <int DT, int BN, int ST, int KA = 1>
 Variant make_tc_variant() {
-  using Cfg = TcConfig<DT, BN, ST>;
+  using Cfg = TcConfig<DT, BN, ST, KA>;
   Variant v;
   v.path = Path::kTensor;
   v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc<Cfg>);
@@ -79,21 +81,23 @@ Variant make_tc_variant() {
   v.elem = Cfg::ELEM;
   v.b_chunk_n = Cfg::B_CHUNK_N;
   v.a_box_rows = Cfg::BM;
+  v.a_box_k = Cfg::ATOM_K;
+  v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 1;
-  v.launch_tc = &launch_tc_impl<DT, BN, ST>;
+  v.launch_tc = &launch_tc_impl<DT, BN, ST, KA>;
   return v;
 }
 
-template <int DT, int ST>
+template <int DT, int ST, int KA>
 void launch_tc2_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                      const TcParams &p) {
-  using Cfg = pf::Tc2Config<DT, ST>;
+  using Cfg = pf::Tc2Config<DT, ST, KA>;
   pf::gemm_bias_gelu_tc2<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
 }
 
-template <int DT, int ST>
+template <int DT, int ST, int KA = 1>
 Variant make_tc2_variant() {
-  using Cfg = pf::Tc2Config<DT, ST>;
+  using Cfg = pf::Tc2Config<DT, ST, KA>;
   Variant v;
   v.path = Path::kTensor;
   v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc2<Cfg>);
@@ -106,8 +110,10 @@ Variant make_tc2_variant() {
   v.elem = Cfg::ELEM;
   v.b_chunk_n = Cfg::B_CHUNK_N;
   v.a_box_rows = Cfg::BM_CTA;
+  v.a_box_k = Cfg::ATOM_K;
+  v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 2;
-  v.launch_tc = &launch_tc2_impl<DT, ST>;
+  v.launch_tc = &launch_tc2_impl<DT, ST, KA>;
   return v;
 }
 
@@ -158,27 +164,32 @@ bool same_tile(const pf_tile &a, const pf_tile &b) {
   return a.BM == b.BM && a.BN == b.BN && a.BK == b.BK && a.TM == b.TM && a.TN == b.TN && a.PAD == b.PAD;
 }
 
-// Tensor-path variant for (dtype, BM, BN, requested pipeline depth TM).  The depth is clamped to the
-// deepest compiled variant that fits in shared memory (TM=8 asks for "as deep as fits").
-bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, Variant *out) {
+// Tensor-path variant for (dtype, BM, BN, requested pipeline depth TM, k-atoms per stage).  The depth is
+// clamped to the deepest compiled variant that fits in shared memory (TM=8 asks for "as deep as fits").
+bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant *out) {
   struct Entry {
-    int dt, bm, bn, stages;
+    int dt, bm, bn, stages, katoms;
     Variant (*make)();
   };
   static const Entry table[] = {
-      {PF_BF16, 128, 256, 2, &make_tc_variant<0, 256, 2>},  {PF_BF16, 128, 256, 4, &make_tc_variant<0, 256, 4>},
-      {PF_BF16, 128, 128, 2, &make_tc_variant<0, 128, 2>},  {PF_BF16, 128, 128, 4, &make_tc_variant<0, 128, 4>},
-      {PF_BF16, 128, 128, 6, &make_tc_variant<0, 128, 6>},  {PF_BF16, 128, 64, 4, &make_tc_variant<0, 64, 4>},
-      {PF_BF16, 128, 64, 8, &make_tc_variant<0, 64, 8>},    {PF_BF16, 256, 256, 2, &make_tc2_variant<0, 2>},
-      {PF_BF16, 256, 256, 4, &make_tc2_variant<0, 4>},      {PF_BF16, 256, 256, 6, &make_tc2_variant<0, 6>},
-      {PF_E4M3, 128, 256, 2, &make_tc_variant<1, 256, 2>},  {PF_E4M3, 128, 256, 4, &make_tc_variant<1, 256, 4>},
-      {PF_E4M3, 128, 128, 2, &make_tc_variant<1, 128, 2>},  {PF_E4M3, 128, 128, 4, &make_tc_variant<1, 128, 4>},
-      {PF_E4M3, 128, 128, 6, &make_tc_variant<1, 128, 6>},  {PF_E4M3, 256, 256, 2, &make_tc2_variant<1, 2>},
-      {PF_E4M3, 256, 256, 4, &make_tc2_variant<1, 4>},      {PF_E4M3, 256, 256, 6, &make_tc2_variant<1, 6>},
+      {PF_BF16, 128, 256, 2, 1, &make_tc_variant<0, 256, 2>},     {PF_BF16, 128, 256, 4, 1, &make_tc_variant<0, 256, 4>},
+      {PF_BF16, 128, 256, 2, 2, &make_tc_variant<0, 256, 2, 2>},  {PF_BF16, 128, 128, 2, 1, &make_tc_variant<0, 128, 2>},
+      {PF_BF16, 128, 128, 4, 1, &make_tc_variant<0, 128, 4>},     {PF_BF16, 128, 128, 6, 1, &make_tc_variant<0, 128, 6>},
+      {PF_BF16, 128, 128, 3, 2, &make_tc_variant<0, 128, 3, 2>},  {PF_BF16, 128, 64, 4, 1, &make_tc_variant<0, 64, 4>},
+      {PF_BF16, 128, 64, 8, 1, &make_tc_variant<0, 64, 8>},       {PF_BF16, 256, 256, 2, 1, &make_tc2_variant<0, 2>},
+      {PF_BF16, 256, 256, 4, 1, &make_tc2_variant<0, 4>},         {PF_BF16, 256, 256, 6, 1, &make_tc2_variant<0, 6>},
+      {PF_BF16, 256, 256, 3, 2, &make_tc2_variant<0, 3, 2>},      {PF_E4M3, 128, 256, 2, 1, &make_tc_variant<1, 256, 2>},
+      {PF_E4M3, 128, 256, 4, 1, &make_tc_variant<1, 256, 4>},     {PF_E4M3, 128, 256, 2, 2, &make_tc_variant<1, 256, 2, 2>},
+      {PF_E4M3, 128, 128, 2, 1, &make_tc_variant<1, 128, 2>},     {PF_E4M3, 128, 128, 4, 1, &make_tc_variant<1, 128, 4>},
+      {PF_E4M3, 128, 128, 6, 1, &make_tc_variant<1, 128, 6>},     {PF_E4M3, 256, 256, 2, 1, &make_tc2_variant<1, 2>},
+      {PF_E4M3, 256, 256, 4, 1, &make_tc2_variant<1, 4>},         {PF_E4M3, 256, 256, 6, 1, &make_tc2_variant<1, 6>},
+      {PF_E4M3, 256, 256, 3, 2, &make_tc2_variant<1, 3, 2>},
   };
   const Entry *best = nullptr;
   for (const Entry &e : table)
-    if (e.dt == dt && e.bm == bm && e.bn == bn && e.stages <= depth && (!best || e.stages > best->stages)) best = &e;
+    if (e.dt == dt && e.bm == bm && e.bn == bn && e.katoms == katoms && e.stages <= depth &&
+        (!best || e.stages > best->stages))
+      best = &e;
   if (!best) return false;
   *out = best->make();
   return true;
@@ -286,7 +297,7 @@ int encode_maps(pf_ctx *c) {
   const uint64_t e = static_cast<uint64_t>(v.elem);
   int rc;
   // A: [M x K], K contiguous; box = BK elements (128 B) x BM rows.
-  rc = encode_2d(c, &c->tmA, in_t, c->A, c->K, c->M, c->K * e, v.bk_elems, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_2d(c, &c->tmA, in_t, c->A, c->K, c->M, c->K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   // B: [K x N], N contiguous; box = 128 B of N x BK rows.
   rc = encode_2d(c, &c->tmB, in_t, c->B, c->N, c->K, c->N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -430,9 +441,10 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
       return set_err(c, PF_ETILE, "tensor path: BM must be 128 (one CTA) or 256 (CTA pair), got %d", t->BM);
     if (t->BK != 32)
       return set_err(c, PF_ETILE, "tensor path: BK must be 32 words (one 128-byte swizzle row), got %d", t->BK);
-    if (t->PAD != 0) return set_err(c, PF_ETILE, "tensor path: PAD must be 0, got %d", t->PAD);
+    if (t->PAD != 0 && t->PAD != 1)
+      return set_err(c, PF_ETILE, "tensor path: PAD (extra 128-byte k-atoms per stage) must be 0 or 1, got %d", t->PAD);
     if (t->TN < 1 || t->TN > 64) return set_err(c, PF_ETILE, "tensor path: TN (raster group) out of range: %d", t->TN);
-    if (!find_tc_variant(dt, t->BM, t->BN, t->TM, &v))
+    if (!find_tc_variant(dt, t->BM, t->BN, t->TM, t->PAD + 1, &v))
       return set_err(c, PF_ETILE, "tensor path: no %s kernel with BM=%d, BN=%d and at most %d stages",
                      dt == PF_BF16 ? "bf16" : "e4m3", t->BM, t->BN, t->TM);
     const int e = (int)pf_elem_bytes(dt);
@@ -764,11 +776,11 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   if (d.cc_major != 10) return noalloc_fail(err, err_len, PF_ENODEV, "device %d is not an sm_100 GPU", device);
 
   // Kernel variant and layout rules: those of pf_prepare / pf_bind.
-  if ((t->BM != 128 && t->BM != 256) || t->BK != 32 || t->PAD != 0 || t->TN < 1 || t->TN > 64)
+  if ((t->BM != 128 && t->BM != 256) || t->BK != 32 || (t->PAD != 0 && t->PAD != 1) || t->TN < 1 || t->TN > 64)
     return noalloc_fail(err, err_len, PF_ETILE, "tile %dx%dx%d t%dx%d p%d has no tensor-core kernel", t->BM, t->BN,
                         t->BK, t->TM, t->TN, t->PAD);
   Variant v;
-  if (!find_tc_variant(dtype, t->BM, t->BN, t->TM, &v))
+  if (!find_tc_variant(dtype, t->BM, t->BN, t->TM, t->PAD + 1, &v))
     return noalloc_fail(err, err_len, PF_ETILE, "no kernel with BM=%d, BN=%d and at most %d stages", t->BM, t->BN,
                         t->TM);
   const long long e = static_cast<long long>(pf_elem_bytes(dtype));
@@ -808,7 +820,7 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   const CUtensorMapDataType in_t =
       dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUtensorMap tmA, tmB, tmC;
-  if (encode_2d(nullptr, &tmA, in_t, A, K, M, K * e, v.bk_elems, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (encode_2d(nullptr, &tmA, in_t, A, K, M, K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
       encode_2d(nullptr, &tmB, in_t, B, N, K, N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B) ||
       encode_2d(nullptr, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
     return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");

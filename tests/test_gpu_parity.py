@@ -140,9 +140,11 @@ def test_fp32_cfg2_gate_and_torch(ctx, oracle_mod):
 # ---------------------------------------------------------------------------------------------
 BF16_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
               (128, 128, 32, 8, 8, 0), (128, 64, 32, 8, 16, 0), (128, 64, 32, 4, 2, 0),
-              (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0), (256, 256, 32, 2, 8, 0)]
+              (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0), (256, 256, 32, 2, 8, 0),
+              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1), (128, 128, 32, 8, 8, 1)]
 E4M3_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
-              (128, 128, 32, 8, 4, 0), (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0)]
+              (128, 128, 32, 8, 4, 0), (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0),
+              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1)]
 
 
 @pytest.mark.parametrize("tile", BF16_TILES)
@@ -223,13 +225,15 @@ def test_run_host_equals_device_path(ctx, pf):
 def test_timing_protocol_and_attrs(ctx):
     w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 1024, 1024, 1024)
     inp = wl.make_inputs(w)
-    run_pf(ctx, w, inp)
-    ms = ctx.time(warmup=2, iters=5, reps=3)
-    assert 0 < ms < 50
-    a = ctx.attrs()
-    # local_bytes is the per-thread stack frame (8 B of bookkeeping); ptxas reports 0 bytes of spills
-    assert a["threads"] == 192 and a["blocks_per_sm"] == 1 and a["local_bytes"] <= 16
-    assert a["num_sms"] == 148 and a["grid"] == min(a["num_sms"], (1024 // 128) * (1024 // 256))
+    for tile, tiles, per_tile in (((128, 256, 32, 4, 16, 0), (1024 // 128) * (1024 // 256), 1),
+                                  ((256, 256, 32, 8, 8, 1), (1024 // 256) * (1024 // 256), 2)):
+        run_pf(ctx, w, inp, tile)
+        ms = ctx.time(warmup=2, iters=5, reps=3)
+        assert 0 < ms < 50
+        a = ctx.attrs()
+        # local_bytes is the per-thread stack frame (8 B of bookkeeping); ptxas reports 0 bytes of spills
+        assert a["threads"] == 192 and a["blocks_per_sm"] == 1 and a["local_bytes"] <= 16
+        assert a["num_sms"] == 148 and a["grid"] == min(a["num_sms"] // per_tile, tiles) * per_tile
 
 
 def test_invalid_configs_are_errors(ctx, pf):
