@@ -95,6 +95,20 @@ int pf_close(pf_ctx *ctx);
  * per-trial compile + module load (cuda_runner.cpp:159-161, 219-237). */
 int pf_prepare(pf_ctx *ctx, pf_dtype dtype, const pf_tile *tile, int M, int N, int K);
 
+/* Load a kernel image -- PTX text (NUL-terminated or not) or an sm_100a cubin -- whose entry point
+ * `kernel` has the reference kernel ABI
+ *     extern "C" __global__ void kernel(const float *A, const float *B, const float *bias, float *C,
+ *                                       int M, int N, int K)        (kernels/gemm_bias_gelu.cu:42-44)
+ * and prepare it for an fp32 M x N x K problem launched on grid (grid_x, grid_y) with `block` threads.
+ * Afterwards pf_bind / pf_upload / pf_launch / pf_time / pf_attrs / pf_download work as for a
+ * prepared fp32 tile.  A block larger than the kernel allows is refused (PF_ETILE), as in
+ * cuda_runner.cpp:171-175.  Replaces CudaRunner::run_ptx (core/include/ptxforge/cuda_runner.hpp:41-42,
+ * core/src/cuda_runner.cpp:152-217, 251-253): any image -- the reference's own kernel, an
+ * MLIR-generated one, or this library's fp32 kernel JIT-compiled for a tile (simt_image.cu) -- goes
+ * through the same launch, gate and timing. */
+int pf_prepare_image(pf_ctx *ctx, const void *image, size_t image_bytes, const char *kernel, int grid_x,
+                     int grid_y, int block, int M, int N, int K);
+
 /* Bind caller-owned device operands (row-major).  A/B are float, bf16 or e4m3 bytes according to
  * the prepared dtype; C is float for PF_F32 and bf16 otherwise.  scale_a/scale_b are the
  * per-tensor dequantisation scales (used by PF_E4M3, must be 1 otherwise).  Replaces the

@@ -23,8 +23,11 @@
 #include <barrier>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <mutex>
 #include <random>
 #include <sstream>
 #include <string>
@@ -64,7 +67,12 @@ class B200Runner : public Runner {
     int warmup = 5, iters = 20, reps = 5, samples = 512;  // cuda_runner.hpp:29 defaults
     uint64_t seed = 0;
     double tolerance = 0;      // 0: 1e-5 fp32, 2e-2 bf16, 5e-2 e4m3
-    std::string root = ".";    // repository root, for the kernel sources shown by stages()
+    std::string root = ".";    // repository root: kernel sources for stages() and the fp32 JIT
+    // fp32 tiles that libpf_b200.so does not carry precompiled are compiled per trial with nvcc and
+    // loaded through pf_prepare_image, cached on disk (cuda_runner.hpp:28, cuda_runner.cpp:219-237).
+    bool jit = true;
+    std::string nvcc = "nvcc";
+    std::string workdir = "build/kernels";
   };
 
   explicit B200Runner(Options o) : opt_(std::move(o)) {
@@ -124,8 +132,17 @@ class B200Runner : public Runner {
       run_shards(G, [&](int g) {
         if (rows[g] == 0) return;
         pf_ctx *c = ctx_[g];
-        int r;
-        if ((r = pf_prepare(c, opt_.dtype, &tile, rows[g], p.N, p.K))) return fail(g, r);
+        int r = pf_prepare(c, opt_.dtype, &tile, rows[g], p.N, p.K);
+        if (r == PF_ETILE && opt_.dtype == PF_F32 && opt_.jit) {
+          std::string jerr;
+          r = prepare_jit(c, cfg, rows[g], p, jerr);
+          if (r && !jerr.empty()) {
+            rc[g] = r;
+            err[g] = jerr;
+            return;
+          }
+        }
+        if (r) return fail(g, r);
         if ((r = pf_upload(c, hA_.data() + static_cast<size_t>(row0[g]) * p.K * e, hB_.data(), hbias_.data(), sa_,
                            sb_)))
           return fail(g, r);
@@ -206,6 +223,50 @@ class B200Runner : public Runner {
   const Options &options() const { return opt_; }
 
  private:
+  // nvcc the fp32 SIMT kernel (ptxforge_b200/csrc/simt_image.cu, reference kernel ABI) for this tile
+  // into workdir (cached; serialised across shard threads) and load it with pf_prepare_image on the
+  // reference launch shape: grid (ceil(N/BN), ceil(rows/BM)), block (BM/TM)*(BN/TN).
+  int prepare_jit(pf_ctx *c, const Config &cfg, int rows, const Problem &p, std::string &err) {
+    const std::string name = "simt_" + std::to_string(cfg.BM) + "_" + std::to_string(cfg.BN) + "_" +
+                             std::to_string(cfg.BK) + "_" + std::to_string(cfg.TM) + "_" + std::to_string(cfg.TN) +
+                             "_" + std::to_string(cfg.PAD) + ".cubin";
+    const std::string path = opt_.workdir + "/" + name;
+    std::string image;
+    {
+      std::lock_guard<std::mutex> lock(jit_mutex_);
+      std::ifstream probe(path, std::ios::binary);
+      if (!probe) {
+        std::string mk = "mkdir -p '" + opt_.workdir + "'";
+        if (std::system(mk.c_str()) != 0) {
+          err = "cannot create " + opt_.workdir;
+          return PF_ETILE;
+        }
+        const std::string src = opt_.root + "/ptxforge_b200/csrc/simt_image.cu";
+        std::string cmd = opt_.nvcc + " -cubin -gencode arch=compute_100a,code=sm_100a -O3 -lineinfo";
+        for (const auto &d : cfg.defines()) cmd += " " + d;
+        cmd += " -I '" + opt_.root + "/ptxforge_b200/csrc' '" + src + "' -o '" + path + ".tmp' 2>&1";
+        std::string log;
+        FILE *pipe = popen(cmd.c_str(), "r");
+        if (!pipe) {
+          err = "cannot run nvcc";
+          return PF_ETILE;
+        }
+        char buf[4096];
+        size_t n;
+        while ((n = fread(buf, 1, sizeof buf, pipe)) > 0) log.append(buf, n);
+        if (pclose(pipe) != 0) {
+          std::remove((path + ".tmp").c_str());
+          err = "nvcc failed: " + log.substr(log.size() > 800 ? log.size() - 800 : 0);
+          return PF_ETILE;
+        }
+        std::rename((path + ".tmp").c_str(), path.c_str());
+      }
+      image = read_file(path);
+    }
+    const int gx = (p.N + cfg.BN - 1) / cfg.BN, gy = (rows + cfg.BM - 1) / cfg.BM;
+    return pf_prepare_image(c, image.data(), image.size(), "gemm_bias_gelu", gx, gy, cfg.threads(), rows, p.N, p.K);
+  }
+
   static std::string hex(unsigned v) {
     std::ostringstream s;
     s << std::hex << v;
@@ -370,6 +431,7 @@ class B200Runner : public Runner {
   std::vector<uint8_t> hA_, hB_, hC_;
   std::vector<float> hbias_, vbias_, vA_, vB_;
   float sa_ = 1.f, sb_ = 1.f;
+  std::mutex jit_mutex_;
 };
 
 }  // namespace ptxforge

@@ -181,6 +181,11 @@ def ref_kernel_path(name: str) -> str:
     return _build.ref_kernel_lib(name)
 
 
+def ref_kernel_cubin(name: str) -> str:
+    """The reference's fp32 kernel compiled to an sm_100a cubin (what CudaRunner would load)."""
+    return _build.ref_kernel_cubin(name)
+
+
 def ref_kernel(name: str):
     """ctypes handle of the reference's fp32 kernel built for sm_100a (GPU only)."""
     L = ctypes.CDLL(ref_kernel_path(name))

@@ -8,6 +8,8 @@ Outputs
                                         compiled from its own source with the reference's own flags
                                         (tests/fake_cuda/run.sh:14); its cuLaunchKernel is the fp64 result
                                         the reference's tests accept as correct
+  oracle/_ref/gemm_bias_gelu_ref_<cfg>.cubin  the same kernel as an image, compiled as CudaRunner does
+                                        (cuda_runner.cpp:228-230), for the image path (pf_prepare_image)
   oracle/_ref/libref_kernel_<cfg>.so    the reference's fp32 kernel (kernels/gemm_bias_gelu.cu) compiled
                                         for sm_100a at a tile config, behind oracle/ref_kernel_launch.cu
 
@@ -65,6 +67,10 @@ def ref_kernel_lib(name: str) -> str:
 FAKECUDA = os.path.join(REF_DIR, "libfakecuda_ref.so")
 
 
+def ref_kernel_cubin(name: str) -> str:
+    return os.path.join(REF_DIR, f"gemm_bias_gelu_ref_{name}.cubin")
+
+
 def build_ref(force: bool = False) -> list[str]:
     """Compile the reference's own code (when the reference tree is present) into oracle/_ref/."""
     if not os.path.isdir(REF_ROOT):
@@ -80,6 +86,15 @@ def build_ref(force: bool = False) -> list[str]:
     kern_src = os.path.join(REF_ROOT, "kernels", "gemm_bias_gelu.cu")
     launcher = os.path.join(HERE, "ref_kernel_launch.cu")
     if os.path.exists(kern_src):
+        # the reference kernel as an image, compiled the way CudaRunner compiles it
+        # (cuda_runner.cpp:228-230: nvcc -cubin -arch=<arch> -O3 -lineinfo -D<tile>)
+        for name, cfg in REF_KERNEL_CONFIGS.items():
+            cub = ref_kernel_cubin(name)
+            if force or _stale(cub, [kern_src]):
+                defs = [f"-D{k}={v}" for k, v in cfg.items()]
+                _run([os.path.join(CUDA_HOME, "bin", "nvcc"), "-cubin", "-arch=sm_100a", "-O3", "-lineinfo", *defs,
+                      kern_src, "-o", cub])
+            out.append(cub)
         for name, cfg in REF_KERNEL_CONFIGS.items():
             lib = ref_kernel_lib(name)
             if force or _stale(lib, [kern_src, launcher]):

@@ -30,7 +30,7 @@ OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
 SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
            "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
-           "pf_gemm_bias_gelu_noalloc")
+           "pf_gemm_bias_gelu_noalloc", "pf_prepare_image")
 
 
 class Tile(ctypes.Structure):
@@ -99,6 +99,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
         lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_download.argtypes = [vp, vp]
+        lib.pf_prepare_image.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, i, i, i, i, i, i]
         lib.pf_gemm_bias_gelu_noalloc.argtypes = [i, i, ctypes.POINTER(Tile), i, i, i, vp, vp, vp, vp, ctypes.c_float,
                                                   ctypes.c_float, vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p,
                                                   ctypes.c_size_t]
@@ -110,7 +111,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_selftest_wait_timeout.argtypes = [vp, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
-                     "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc"):
+                     "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc",
+                     "pf_prepare_image"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -183,6 +185,13 @@ class Context:
         t = tile if isinstance(tile, Tile) else Tile(*(tile or DEFAULT_TILES[dtype]))
         self._check(self._lib.pf_prepare(self._h, DTYPES[dtype], ctypes.byref(t), M, N, K), "pf_prepare")
         self.dtype, self.shape, self.tile = dtype, (M, N, K), t
+        return self
+
+    def prepare_image(self, image: bytes, kernel: str, grid: tuple[int, int], block: int, M: int, N: int, K: int):
+        """Load a PTX/cubin image with the reference kernel ABI (pf_prepare_image, the run_ptx path)."""
+        self._check(self._lib.pf_prepare_image(self._h, image, len(image), kernel.encode(), grid[0], grid[1], block,
+                                               M, N, K), "pf_prepare_image")
+        self.dtype, self.shape, self.tile = "f32", (M, N, K), None
         return self
 
     def bind(self, A, B, bias, C, scale_a: float = 1.0, scale_b: float = 1.0):

@@ -51,10 +51,12 @@ __device__ __forceinline__ int micro_index(int ty, int i) {
   }
 }
 
+// The kernel body, shared by the templated kernel below and by the standalone image with the
+// reference ABI (simt_image.cu).
 template <int BM, int BN, int BK, int TM, int TN, int PAD, bool VEC>
-__global__ void __launch_bounds__(SimtConfig<BM, BN, BK, TM, TN, PAD>::THREADS)
-    gemm_bias_gelu_simt(const float *__restrict__ A, const float *__restrict__ B, const float *__restrict__ bias,
-                        float *__restrict__ C, int M, int N, int K) {
+__device__ __forceinline__ void gemm_bias_gelu_simt_body(const float *__restrict__ A, const float *__restrict__ B,
+                                                         const float *__restrict__ bias, float *__restrict__ C,
+                                                         int M, int N, int K) {
   using Cfg = SimtConfig<BM, BN, BK, TM, TN, PAD>;
   __shared__ __align__(16) float As[2][BK][BM + PAD];  // transposed: As[k][m]
   __shared__ __align__(16) float Bs[2][BK][BN];
@@ -215,6 +217,13 @@ __global__ void __launch_bounds__(SimtConfig<BM, BN, BK, TM, TN, PAD>::THREADS)
       }
     }
   }
+}
+
+template <int BM, int BN, int BK, int TM, int TN, int PAD, bool VEC>
+__global__ void __launch_bounds__(SimtConfig<BM, BN, BK, TM, TN, PAD>::THREADS)
+    gemm_bias_gelu_simt(const float *__restrict__ A, const float *__restrict__ B, const float *__restrict__ bias,
+                        float *__restrict__ C, int M, int N, int K) {
+  gemm_bias_gelu_simt_body<BM, BN, BK, TM, TN, PAD, VEC>(A, B, bias, C, M, N, K);
 }
 
 }  // namespace pf

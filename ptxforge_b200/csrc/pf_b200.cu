@@ -36,7 +36,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-enum class Path { kNone, kSimt, kTensor };
+enum class Path { kNone, kSimt, kTensor, kImage };
 
 // Launch description of one compiled variant.
 struct Variant {
@@ -53,6 +53,9 @@ struct Variant {
   int b_chunk_n = 0;
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                     const TcParams &) = nullptr;
+  // image path (pf_prepare_image): a loaded kernel with the reference ABI
+  CUfunction img_fn = nullptr;
+  int img_gx = 0, img_gy = 0;
   // simt path
   int sbm = 0, sbn = 0;
   void (*launch_simt)(dim3, cudaStream_t, const float *, const float *, const float *, float *, int, int, int,
@@ -195,6 +198,45 @@ bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant
   return true;
 }
 
+// Driver entry points of the image path, fetched through the runtime (no link-time libcuda).
+struct DriverApi {
+  CUresult (*moduleLoadData)(CUmodule *, const void *) = nullptr;
+  CUresult (*moduleUnload)(CUmodule) = nullptr;
+  CUresult (*moduleGetFunction)(CUfunction *, CUmodule, const char *) = nullptr;
+  CUresult (*launchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
+                           void **, void **) = nullptr;
+  CUresult (*funcGetAttribute)(int *, CUfunction_attribute, CUfunction) = nullptr;
+  CUresult (*occupancy)(int *, CUfunction, int, size_t) = nullptr;
+  CUresult (*getErrorString)(CUresult, const char **) = nullptr;
+  bool ok = false;
+};
+
+const DriverApi &driver_api() {
+  static DriverApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    auto get = [](const char *name, void **fn) {
+      cudaDriverEntryPointQueryResult q;
+      return cudaGetDriverEntryPointByVersion(name, fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+             q == cudaDriverEntryPointSuccess;
+    };
+    api.ok = get("cuModuleLoadData", reinterpret_cast<void **>(&api.moduleLoadData)) &&
+             get("cuModuleUnload", reinterpret_cast<void **>(&api.moduleUnload)) &&
+             get("cuModuleGetFunction", reinterpret_cast<void **>(&api.moduleGetFunction)) &&
+             get("cuLaunchKernel", reinterpret_cast<void **>(&api.launchKernel)) &&
+             get("cuFuncGetAttribute", reinterpret_cast<void **>(&api.funcGetAttribute)) &&
+             get("cuOccupancyMaxActiveBlocksPerMultiprocessor", reinterpret_cast<void **>(&api.occupancy)) &&
+             get("cuGetErrorString", reinterpret_cast<void **>(&api.getErrorString));
+  });
+  return api;
+}
+
+const char *cu_err(CUresult r) {
+  const char *s = nullptr;
+  if (driver_api().getErrorString) driver_api().getErrorString(r, &s);
+  return s ? s : "unknown CUDA driver error";
+}
+
 EncodeTiledFn get_encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static bool tried = false;
@@ -234,6 +276,7 @@ struct pf_ctx {
   float sa = 1.f, sb = 1.f;
   CUtensorMap tmA{}, tmB{}, tmC{};
   bool simt_vec = false;
+  CUmodule module = nullptr;  // image loaded by pf_prepare_image
 
   // pf_run_host buffers
   void *hbufA = nullptr, *hbufB = nullptr, *hbufC = nullptr;
@@ -330,6 +373,16 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     p.timeout_ns = c->timeout_ns;
     dim3 grid(std::min(p.num_tiles, c->max_units) * v.cta_per_tile);
     v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, p);
+  } else if (v.path == Path::kImage) {
+    // The reference's parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} (cuda_runner.cpp:182).
+    const void *a = c->A, *b = c->B, *bias = c->bias;
+    void *cc = c->C;
+    int M = c->M, N = c->N, K = c->K;
+    void *params[] = {&a, &b, &bias, &cc, &M, &N, &K};
+    CUresult r = driver_api().launchKernel(v.img_fn, static_cast<unsigned>(v.img_gx), static_cast<unsigned>(v.img_gy),
+                                           1, static_cast<unsigned>(v.threads), 1, 1, 0,
+                                           reinterpret_cast<CUstream>(s), params, nullptr);
+    if (r != CUDA_SUCCESS) return set_err(c, PF_ECUDA, "cuLaunchKernel -> %s", cu_err(r));
   } else {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (c->M + v.sbm - 1) / v.sbm);
     v.launch_simt(grid, s, static_cast<const float *>(c->A), static_cast<const float *>(c->B), c->bias,
@@ -405,8 +458,56 @@ int pf_close(pf_ctx *c) {
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
     if (c->stream) cudaStreamDestroy(c->stream);
+    if (c->module) driver_api().moduleUnload(c->module);
   }
   delete c;
+  return PF_OK;
+}
+
+int pf_prepare_image(pf_ctx *c, const void *image, size_t image_bytes, const char *kernel, int grid_x, int grid_y,
+                     int block, int M, int N, int K) {
+  if (!c || !image || !image_bytes || !kernel) return set_err(c, PF_EINVAL, "null argument");
+  c->prepared = false;
+  c->bound = false;
+  if (M <= 0 || N <= 0 || K <= 0 || grid_x <= 0 || grid_y <= 0 || block <= 0)
+    return set_err(c, PF_EINVAL, "sizes and launch shape must be positive");
+  const DriverApi &api = driver_api();
+  if (!api.ok) return set_err(c, PF_ECUDA, "CUDA driver entry points unavailable");
+  DeviceGuard g(c->device);
+  if (c->module) {
+    api.moduleUnload(c->module);
+    c->module = nullptr;
+  }
+  // PTX must be NUL-terminated; a cubin is unaffected by a trailing byte (cuda_runner.cpp:157).
+  std::string img(static_cast<const char *>(image), image_bytes);
+  img.push_back('\0');
+  CUresult r = api.moduleLoadData(&c->module, img.data());
+  if (r != CUDA_SUCCESS) {
+    c->module = nullptr;
+    return set_err(c, PF_ECUDA, "cuModuleLoadData -> %s", cu_err(r));
+  }
+  CUfunction fn = nullptr;
+  if ((r = api.moduleGetFunction(&fn, c->module, kernel)) != CUDA_SUCCESS)
+    return set_err(c, PF_ECUDA, "cuModuleGetFunction(%s) -> %s", kernel, cu_err(r));
+  int max_block = 0;
+  if ((r = api.funcGetAttribute(&max_block, CU_FUNC_ATTRIBUTE_MAX_THREADS_PER_BLOCK, fn)) != CUDA_SUCCESS)
+    return set_err(c, PF_ECUDA, "cuFuncGetAttribute -> %s", cu_err(r));
+  if (block > max_block)
+    return set_err(c, PF_ETILE, "block %d exceeds kernel max %d (register pressure)", block, max_block);
+  Variant v;
+  v.path = Path::kImage;
+  v.img_fn = fn;
+  v.img_gx = grid_x;
+  v.img_gy = grid_y;
+  v.threads = block;
+  c->var = v;
+  c->dtype = PF_F32;
+  c->tile = pf_tile{0, 0, 0, 0, 0, 0};
+  c->M = M;
+  c->N = N;
+  c->K = K;
+  c->prepared = true;
+  c->err.clear();
   return PF_OK;
 }
 
@@ -556,6 +657,24 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
   if (!c || !out) return PF_EINVAL;
   if (!c->prepared) return set_err(c, PF_ESTATE, "pf_attrs before pf_prepare");
   DeviceGuard g(c->device);
+  if (c->var.path == Path::kImage) {
+    const DriverApi &api = driver_api();
+    int regs = 0, local = 0, smem = 0, bps = 0;
+    CUresult r;
+    if ((r = api.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, c->var.img_fn)) != CUDA_SUCCESS ||
+        (r = api.funcGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, c->var.img_fn)) != CUDA_SUCCESS ||
+        (r = api.funcGetAttribute(&smem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, c->var.img_fn)) != CUDA_SUCCESS ||
+        (r = api.occupancy(&bps, c->var.img_fn, c->var.threads, 0)) != CUDA_SUCCESS)
+      return set_err(c, PF_ECUDA, "kernel attributes -> %s", cu_err(r));
+    out->regs = regs;
+    out->local_bytes = local;
+    out->smem_bytes = smem;
+    out->blocks_per_sm = bps;
+    out->threads = c->var.threads;
+    out->num_sms = c->num_sms;
+    out->grid = c->var.img_gx * c->var.img_gy;
+    return PF_OK;
+  }
   cudaFuncAttributes fa;
   PF_CUDA(c, cudaFuncGetAttributes(&fa, c->var.func));
   int bps = 0;

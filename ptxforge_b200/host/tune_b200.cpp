@@ -64,6 +64,9 @@ B200Runner::Options runner_options(const Args &a) {
   o.samples = a.geti("samples", 512);
   o.seed = static_cast<uint64_t>(a.geti("seed", 0));
   o.root = a.get("root", ".");
+  o.nvcc = a.get("nvcc", "nvcc");
+  o.workdir = a.get("workdir", "build/kernels");
+  o.jit = a.get("jit", "1") != "0";
   return o;
 }
 

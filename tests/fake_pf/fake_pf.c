@@ -105,7 +105,18 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     if (t->TM < 2) return set_err(c, PF_ETILE, "tensor path: no kernel with %d stages", t->TM);
     const int e = (int)pf_elem_bytes(dt);
     if ((K * e) % 16 || (N * e) % 16 || (N * 2) % 16) return set_err(c, PF_ESHAPE, "rows must be multiples of 16 bytes");
-  } else if (dt != PF_F32) {
+  } else if (dt == PF_F32) {
+    /* the fp32 tiles the real library carries precompiled */
+    static const int known[][6] = {{128, 128, 8, 8, 8, 4}, {128, 128, 8, 8, 8, 0}, {128, 128, 16, 8, 8, 4},
+                                   {128, 64, 8, 8, 4, 4},  {64, 128, 8, 4, 8, 4},  {64, 64, 8, 4, 4, 0},
+                                   {64, 64, 8, 4, 4, 4},   {64, 64, 16, 4, 4, 4},  {32, 64, 8, 2, 4, 4},
+                                   {32, 32, 8, 2, 2, 0}};
+    int found = 0;
+    for (size_t i = 0; i < sizeof known / sizeof known[0]; ++i)
+      found |= known[i][0] == t->BM && known[i][1] == t->BN && known[i][2] == t->BK && known[i][3] == t->TM &&
+               known[i][4] == t->TN && known[i][5] == t->PAD;
+    if (!found) return set_err(c, PF_ETILE, "fp32 tile is not compiled into this library");
+  } else {
     return set_err(c, PF_ETILE, "dtype %d not built", (int)dt);
   }
   c->dtype = dt;
@@ -115,6 +126,22 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
   c->K = K;
   c->prepared = 1;
   c->err[0] = 0;
+  return PF_OK;
+}
+
+int pf_prepare_image(pf_ctx *c, const void *image, size_t image_bytes, const char *kernel, int gx, int gy, int block,
+                     int M, int N, int K) {
+  if (!c || !image || !image_bytes || !kernel) return PF_EINVAL;
+  flog("prepare_image", c->device);
+  c->prepared = c->bound = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || gx <= 0 || gy <= 0 || block <= 0) return set_err(c, PF_EINVAL, "bad sizes");
+  if (block > 1024) return set_err(c, PF_ETILE, "block %d exceeds kernel max 1024 (register pressure)", block);
+  c->dtype = PF_F32;
+  memset(&c->tile, 0, sizeof c->tile);
+  c->M = M;
+  c->N = N;
+  c->K = K;
+  c->prepared = 1;
   return PF_OK;
 }
 

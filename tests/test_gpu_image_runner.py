@@ -1,0 +1,138 @@
+"""The image path (pf_prepare_image, PTXForge's run_ptx) and the C++ runner / tuner on a B200 (-m gpu).
+
+* The reference's own kernel, compiled to an sm_100a cubin the way CudaRunner compiles it, loads, runs and
+  gates through pf_prepare_image, and gives bit for bit the output of this library's fp32 kernel.
+* This library's fp32 kernel JIT-compiled for a tile it does not carry (ptxforge_b200/csrc/simt_image.cu)
+  matches the precompiled tiles bit for bit (every output is fmaf over k in order, whatever the tile).
+* build/ptxforge-tune-b200 (PTXForge's tuner with the B200 runner, built where the PTXForge headers
+  exist) measures bf16, e4m3 and a JIT'd fp32 tile on the real library, shards rows over every visible GPU,
+  and runs a short tune.
+"""
+import json
+import os
+import subprocess
+import tempfile
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from ptxforge_b200 import workloads as wl  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TUNE = os.path.join(ROOT, "build", "ptxforge-tune-b200")
+
+
+def _fp32_ops(w, inp):
+    A = torch.from_numpy(inp.A).cuda()
+    B = torch.from_numpy(inp.B).cuda()
+    bias = torch.from_numpy(inp.bias).cuda()
+    return A, B, bias
+
+
+def _run_tile(ctx, w, A, B, bias, tile):
+    C = torch.full((w.M, w.N), float("nan"), device="cuda")
+    ctx.prepare("f32", tile, w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C)
+    ctx.launch()
+    torch.cuda.synchronize()
+    return C
+
+
+@pytest.mark.parametrize("name,tile", [("default", (64, 64, 8, 4, 4, 0)), ("best5050", (128, 64, 32, 8, 4, 2))])
+def test_reference_kernel_image_runs_and_matches(ctx, oracle_mod, name, tile):
+    cub = oracle_mod.ref_kernel_cubin(name)
+    if not os.path.exists(cub):
+        pytest.skip("oracle/_ref not built")
+    w = wl.CONFIGS["cfg2_f32_2048"]
+    inp = wl.make_inputs(w)
+    A, B, bias = _fp32_ops(w, inp)
+    C_img = torch.full((w.M, w.N), float("nan"), device="cuda")
+    BM, BN, BK, TM, TN, PAD = tile
+    ctx.prepare_image(open(cub, "rb").read(), "gemm_bias_gelu", (w.N // BN, w.M // BM), (BM // TM) * (BN // TN),
+                      w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C_img)
+    ctx.launch()
+    torch.cuda.synchronize()
+    a = ctx.attrs()
+    assert a["threads"] == (BM // TM) * (BN // TN) and a["regs"] > 0 and a["grid"] == (w.N // BN) * (w.M // BM)
+    ms = ctx.time(warmup=2, iters=5, reps=3)
+    assert ms > 0
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, C_img.cpu().numpy(), samples=512, seed=99)
+    assert err <= 1e-5
+    assert torch.equal(C_img, _run_tile(ctx, w, A, B, bias, (128, 128, 8, 8, 8, 4)))
+
+
+def test_jit_image_of_an_uncompiled_tile(ctx, oracle_mod):
+    w = wl.scaled(wl.CONFIGS["cfg1_f32_512"], 384, 320, 256)
+    inp = wl.make_inputs(w, seed=13)
+    A, B, bias = _fp32_ops(w, inp)
+    tile = (64, 32, 16, 4, 2, 4)  # not in the library's precompiled set
+    with tempfile.TemporaryDirectory() as d:
+        cub = os.path.join(d, "k.cubin")
+        defs = [f"-D{k}={v}" for k, v in zip(("BM", "BN", "BK", "TM", "TN", "PAD"), tile)]
+        subprocess.run(["nvcc", "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", *defs, "-I",
+                        os.path.join(ROOT, "ptxforge_b200", "csrc"),
+                        os.path.join(ROOT, "ptxforge_b200", "csrc", "simt_image.cu"), "-o", cub], check=True)
+        image = open(cub, "rb").read()
+    C = torch.full((w.M, w.N), float("nan"), device="cuda")
+    ctx.prepare_image(image, "gemm_bias_gelu", (w.N // 32, w.M // 64), (64 // 4) * (32 // 2), w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C)
+    ctx.launch()
+    torch.cuda.synchronize()
+    ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias)
+    assert oracle_mod.max_rel_err(ref, C.cpu().numpy()) <= 1e-5
+    assert torch.equal(C, _run_tile(ctx, w, A, B, bias, (64, 64, 8, 4, 4, 0)))
+
+
+def test_image_block_larger_than_kernel_allows_is_refused(ctx, pf, oracle_mod):
+    cub = oracle_mod.ref_kernel_cubin("default")
+    if not os.path.exists(cub):
+        pytest.skip("oracle/_ref not built")
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare_image(open(cub, "rb").read(), "gemm_bias_gelu", (8, 8), 2048, 512, 512, 512)
+    assert e.value.code == pf.PF_ETILE and "exceeds kernel max" in str(e.value)
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare_image(b"not an image", "gemm_bias_gelu", (8, 8), 256, 512, 512, 512)
+    assert e.value.code == pf.PF_ECUDA
+
+
+def _tune(args):
+    if not os.path.exists(TUNE):
+        pytest.skip("build/ptxforge-tune-b200 not built (needs the PTXForge headers at build time)")
+    r = subprocess.run([TUNE, *args, "--root", ROOT], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    return r
+
+
+@pytest.mark.parametrize("dtype,extra", [
+    ("bf16", ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "8", "--TN", "8", "--PAD", "1"]),
+    ("e4m3", ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "8", "--TN", "8", "--PAD", "1"]),
+    ("bf16", ["--BM", "128", "--BN", "256", "--BK", "32", "--TM", "4", "--TN", "16", "--PAD", "0"]),
+    ("f32", ["--BM", "64", "--BN", "32", "--BK", "16", "--TM", "4", "--TN", "2", "--PAD", "4"]),  # JIT'd tile
+])
+def test_runner_measure_on_the_real_library(dtype, extra, tmp_path):
+    r = _tune(["measure", "--dtype", dtype, "--M", "2048", "--N", "2048", "--K", "1024", "--workdir",
+               str(tmp_path), *extra])
+    assert r.stdout.strip(), r.stderr
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and j["ok"], j
+    assert j["gflops"] > 0 and j["profile"]["max_err"] < {"bf16": 2e-2, "e4m3": 5e-2, "f32": 1e-5}[dtype]
+
+
+def test_runner_shards_rows_over_all_gpus():
+    n = torch.cuda.device_count()
+    r = _tune(["measure", "--dtype", "bf16", "--M", "4096", "--N", "2048", "--K", "1024", "--gpus", str(n)])
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and j["ok"] and j["gpus"] == n, j
+
+
+def test_runner_tune_trace(tmp_path):
+    out = tmp_path / "trace.json"
+    r = _tune(["tune", "--dtype", "bf16", "--M", "1024", "--N", "1024", "--K", "512", "--budget", "8", "--advisor",
+               "rules", "--out", str(out), "--workdir", str(tmp_path)])
+    assert r.returncode == 0, r.stderr[-2000:]
+    t = json.loads(out.read_text())
+    assert t["source"] == "harness" and len(t["trials"]) == 8
+    assert any(x["ok"] for x in t["trials"]) and t["best_gflops"] > 0

@@ -133,3 +133,26 @@ def test_tune_trace_contract(tune_fake, tmp_path):
     names = [s["name"] for s in t["stages"]]
     assert names == ["CUDA C++ source", "LLVM IR", "PTX"]
     assert ".entry" not in t["stages"][2]["text"]  # no compiler-written PTX embedded
+
+
+def test_fp32_tile_outside_the_library_is_jit_compiled(tune_fake, tmp_path):
+    # (64,32,8,4,4,0) is not precompiled: the runner nvcc's ptxforge_b200/csrc/simt_image.cu for it (as
+    # CudaRunner compiles every config, cuda_runner.cpp:219-237) and loads it through pf_prepare_image.
+    log = tmp_path / "calls.log"
+    work = tmp_path / "kernels"
+    args = ["measure", "--dtype", "f32", "--M", "128", "--N", "64", "--K", "64", "--BM", "64", "--BN", "32", "--BK", "8",
+            "--TM", "4", "--TN", "4", "--PAD", "0", "--root", ROOT, "--workdir", str(work)]
+    r = run(tune_fake, args, FAKE_PF_LOG=log)
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and j["ok"], j
+    assert (work / "simt_64_32_8_4_4_0.cubin").exists()
+    assert "prepare_image" in log.read_text()
+
+
+def test_fp32_tile_that_does_not_compile_is_a_failed_trial(tune_fake, tmp_path):
+    # 2 x 4 x (32*(256+0) + 32*256) = 131 KB of static shared memory: nvcc refuses, the trial fails with its log
+    args = ["measure", "--dtype", "f32", "--M", "256", "--N", "256", "--K", "64", "--BM", "256", "--BN", "256", "--BK",
+            "32", "--TM", "16", "--TN", "16", "--PAD", "0", "--root", ROOT, "--workdir", str(tmp_path / "k")]
+    r = run(tune_fake, args)
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 4 and not j["ok"] and j["error"].startswith("nvcc failed")
