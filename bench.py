@@ -13,7 +13,7 @@ Besides the device-timed `value`, the line carries
   e2e           the same metric through the C ABI's host-buffer call (pf_run_host): H2D of A, B, bias
                 from pinned memory, the kernel, D2H of C, every step
   roofline      achieved TFLOP/s of the kernel over the measured dense bf16 peak
-  comparators   cuBLAS bf16 GEMM alone and cuBLAS + a separate bias+GELU pass (torch), same inputs
+  comparators   cuBLAS GEMM alone and cuBLAS + a separate bias+GELU pass (pf_time_cublas), same inputs
   cpu_baseline  the CPU-lowered schedule (oracle port) on the host cores, on a bounded sample (N=1)
   clocks        SM clock and throttle reasons sampled (NVML) during the timed region
 `--impl reference` times the reference's CPU implementation of the path (the port of its CPU-lowered
@@ -226,38 +226,6 @@ def gate_sampled(torch, A, B, bias, C, scale, tol, n=256, seed=1234):
     return err, err <= tol
 
 
-def comparators(torch, A, B, bias, scale, reps=20):
-    """cuBLAS (through torch) GEMM alone and GEMM followed by a separate bias+GELU pass."""
-    if A.dtype == torch.float8_e4m3fn:
-        sa = torch.tensor(scale, device="cuda")
-        one = torch.tensor(1.0, device="cuda")
-        Bt = B.t().contiguous().t()  # column-major B, as torch._scaled_mm requires
-
-        def gemm():
-            return torch._scaled_mm(A, Bt, scale_a=sa, scale_b=one, out_dtype=torch.bfloat16)
-    else:
-        def gemm():
-            return torch.matmul(A, B)
-
-    def unfused():
-        y = gemm()
-        return torch.nn.functional.gelu(y.float().add_(bias), approximate="tanh").to(y.dtype)
-
-    out = {}
-    for name, fn in (("cublas_gemm_only", gemm), ("cublas_plus_separate_bias_gelu", unfused)):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(reps):
-            fn()
-        e.record()
-        e.synchronize()
-        out[name] = s.elapsed_time(e) / reps
-    return out
-
-
 def cpu_baseline_sample(w, inp, seconds: float):
     """Time the oracle port of the CPU-lowered schedule on a bounded row sample, all host threads."""
     import oracle
@@ -351,8 +319,10 @@ def run_ours(args, dist):
 
     attrs = ctx.attrs()
     comp = None
-    if not args.no_comparators and dist.world == 1 and w.dtype != "f32":
-        comp = comparators(torch, A, B, bias, scale)
+    if not args.no_comparators and dist.world == 1:
+        # the library's cuBLAS comparator (pf_time_cublas) with as many launches as the timed region
+        g_ms, u_ms = ctx.time_cublas(warmup=5, iters=max(20, args.steps // 5), reps=5)
+        comp = {"cublas_gemm_only": g_ms, "cublas_plus_separate_bias_gelu": u_ms}
 
     res = None
     if dist.rank == 0:

@@ -126,6 +126,15 @@ int pf_launch(pf_ctx *ctx, void *stream);
  * context's stream; per-launch time = elapsed/iters; returns the median over reps in ms. */
 int pf_time(pf_ctx *ctx, int warmup, int iters, int reps, double *median_ms);
 
+/* cuBLAS comparator on the bound operands and shape, timed with the pf_time protocol on the context's
+ * stream: `gemm_ms` = cublasLt GEMM alone (what CudaRunner::Impl::measure_cublas times with
+ * cublasSgemm, cuda_runner.cpp:132-149), `unfused_ms` = the same GEMM followed by a separate bias +
+ * GELU kernel (the "cuBLAS + separate epilogue" of scripts/run_ptx_on_gpu.py:88-90).  bf16: bf16 GEMM,
+ * fp32 accumulate; e4m3: fp8 GEMM with the bound per-tensor scales (B is transposed once, untimed,
+ * as cublasLt's fp8 GEMM wants K-major operands); fp32: fp32 GEMM, no TF32.  C is overwritten with the
+ * unfused result.  cublasLt is loaded at run time; PF_ECUDA if it cannot be. */
+int pf_time_cublas(pf_ctx *ctx, int warmup, int iters, int reps, double *gemm_ms, double *unfused_ms);
+
 /* Kernel attributes of the prepared variant. */
 int pf_attrs(pf_ctx *ctx, pf_attr *out);
 

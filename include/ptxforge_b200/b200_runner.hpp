@@ -73,6 +73,9 @@ class B200Runner : public Runner {
     bool jit = true;
     std::string nvcc = "nvcc";
     std::string workdir = "build/kernels";
+    // cuBLAS comparator once per problem (cuda_runner.hpp:28 `cublas`, cuda_runner.cpp:132-149):
+    // Measurement.cublas_gflops = cuBLAS GEMM alone; cuBLAS + separate bias/GELU via cublas_unfused_gflops().
+    bool cublas = true;
   };
 
   explicit B200Runner(Options o) : opt_(std::move(o)) {
@@ -194,6 +197,24 @@ class B200Runner : public Runner {
       m.ok = true;
       m.ms = t;
       m.gflops = p.flops() / (t * 1e6);
+
+      // cuBLAS comparator, once per problem, on the same shards at once (failures leave it unset, as
+      // the reference's measure_cublas does when cuBLAS cannot be created)
+      if (opt_.cublas && !cublas_gflops_) {
+        std::vector<double> g_ms(G, 0.0), u_ms(G, 0.0);
+        std::vector<int> crc(G, PF_OK);
+        std::barrier sync2(G);
+        run_shards(G, [&](int g) {
+          sync2.arrive_and_wait();
+          if (rows[g] == 0) return;
+          crc[g] = pf_time_cublas(ctx_[g], opt_.warmup, opt_.iters, opt_.reps, &g_ms[g], &u_ms[g]);
+        });
+        if (std::all_of(crc.begin(), crc.end(), [](int r) { return r == PF_OK; })) {
+          cublas_gflops_ = p.flops() / (*std::max_element(g_ms.begin(), g_ms.end()) * 1e6);
+          cublas_unfused_gflops_ = p.flops() / (*std::max_element(u_ms.begin(), u_ms.end()) * 1e6);
+        }
+      }
+      m.cublas_gflops = cublas_gflops_;
     } catch (const std::exception &ex) {
       m.ok = false;
       m.error = ex.what();
@@ -221,6 +242,9 @@ class B200Runner : public Runner {
   }
 
   const Options &options() const { return opt_; }
+
+  // cuBLAS GEMM followed by a separate bias + GELU kernel on the current problem (GFLOP/s), if measured.
+  std::optional<double> cublas_unfused_gflops() const { return cublas_unfused_gflops_; }
 
  private:
   // nvcc the fp32 SIMT kernel (ptxforge_b200/csrc/simt_image.cu, reference kernel ABI) for this tile
@@ -333,6 +357,8 @@ class B200Runner : public Runner {
   void ensure(const Problem &p) {
     if (p.M == prob_.M && p.N == prob_.N && p.K == prob_.K && !hA_.empty()) return;
     prob_ = p;
+    cublas_gflops_.reset();
+    cublas_unfused_gflops_.reset();
     const size_t nA = static_cast<size_t>(p.M) * p.K, nB = static_cast<size_t>(p.K) * p.N;
     const size_t e = pf_elem_bytes(opt_.dtype), o = pf_out_bytes(opt_.dtype);
     std::vector<float> A(nA), B(nB);
@@ -432,6 +458,7 @@ class B200Runner : public Runner {
   std::vector<float> hbias_, vbias_, vA_, vB_;
   float sa_ = 1.f, sb_ = 1.f;
   std::mutex jit_mutex_;
+  std::optional<double> cublas_gflops_, cublas_unfused_gflops_;
 };
 
 }  // namespace ptxforge

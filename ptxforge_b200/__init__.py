@@ -30,7 +30,7 @@ OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
 SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
            "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
-           "pf_gemm_bias_gelu_noalloc", "pf_prepare_image")
+           "pf_gemm_bias_gelu_noalloc", "pf_prepare_image", "pf_time_cublas")
 
 
 class Tile(ctypes.Structure):
@@ -100,6 +100,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_download.argtypes = [vp, vp]
         lib.pf_prepare_image.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, i, i, i, i, i, i]
+        dp = ctypes.POINTER(ctypes.c_double)
+        lib.pf_time_cublas.argtypes = [vp, i, i, i, dp, dp]
         lib.pf_gemm_bias_gelu_noalloc.argtypes = [i, i, ctypes.POINTER(Tile), i, i, i, vp, vp, vp, vp, ctypes.c_float,
                                                   ctypes.c_float, vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p,
                                                   ctypes.c_size_t]
@@ -112,7 +114,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
                      "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc",
-                     "pf_prepare_image"):
+                     "pf_prepare_image", "pf_time_cublas"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -207,6 +209,14 @@ class Context:
         ms = ctypes.c_double()
         self._check(self._lib.pf_time(self._h, warmup, iters, reps, ctypes.byref(ms)), "pf_time")
         return ms.value
+
+    def time_cublas(self, warmup: int = 5, iters: int = 20, reps: int = 5) -> tuple[float, float]:
+        """(cuBLAS GEMM alone, cuBLAS GEMM + separate bias/GELU) in ms on the bound operands (pf_time_cublas).
+        C is overwritten with the unfused result."""
+        g, u = ctypes.c_double(), ctypes.c_double()
+        self._check(self._lib.pf_time_cublas(self._h, warmup, iters, reps, ctypes.byref(g), ctypes.byref(u)),
+                    "pf_time_cublas")
+        return g.value, u.value
 
     def attrs(self) -> dict:
         a = Attr()

@@ -278,6 +278,11 @@ struct pf_ctx {
   bool simt_vec = false;
   CUmodule module = nullptr;  // image loaded by pf_prepare_image
 
+  // cuBLAS comparator state (pf_time_cublas): handle, workspace, GEMM output, transposed fp8 B, scales
+  void *lt_handle = nullptr, *lt_ws = nullptr, *lt_D = nullptr, *lt_Bt = nullptr;
+  float *lt_scales = nullptr;
+  size_t lt_ws_cap = 0, lt_D_cap = 0, lt_Bt_cap = 0;
+
   // pf_run_host buffers
   void *hbufA = nullptr, *hbufB = nullptr, *hbufC = nullptr;
   float *hbufBias = nullptr;
@@ -445,11 +450,18 @@ int pf_open(int device, pf_ctx **out) {
   return PF_OK;
 }
 
+}  // extern "C"
+
+void cublas_cmp_release(pf_ctx *c);  // cublas_cmp.cuh
+
+extern "C" {
+
 int pf_close(pf_ctx *c) {
   if (!c) return PF_EINVAL;
   if (c->device >= 0) {
     DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    cublas_cmp_release(c);
     if (c->d_status) cudaFree(c->d_status);
     if (c->hbufA) cudaFree(c->hbufA);
     if (c->hbufB) cudaFree(c->hbufB);
@@ -974,3 +986,8 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   }
   return PF_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// cuBLAS comparator (pf_time_cublas)
+// ------------------------------------------------------------------------------------------------
+#include "cublas_cmp.cuh"

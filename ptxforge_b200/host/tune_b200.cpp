@@ -67,6 +67,7 @@ B200Runner::Options runner_options(const Args &a) {
   o.nvcc = a.get("nvcc", "nvcc");
   o.workdir = a.get("workdir", "build/kernels");
   o.jit = a.get("jit", "1") != "0";
+  o.cublas = a.get("cublas", "1") != "0";
   return o;
 }
 
@@ -112,6 +113,8 @@ int cmd_measure(const Args &a) {
   const Measurement m = runner.measure(c, problem_of(a), hw);
   json::Value j = measurement_json(m);
   j.set("cfg", c.to_json()).set("dtype", pf_dtype_name(ro.dtype)).set("gpus", ro.gpus);
+  const auto unfused = runner.cublas_unfused_gflops();
+  j.set("cublas_unfused_gflops", unfused ? json::Value(*unfused) : json::Value());
   std::puts(j.dump().c_str());
   return m.ok ? 0 : 4;
 }

@@ -278,3 +278,18 @@ def test_torch_convenience_api(pf):
     torch.cuda.synchronize()
     ref = torch_fp32_reference(A, B, bias, 1.0)
     assert max_rel_err_t(ref, C) <= 2e-2
+
+
+@pytest.mark.parametrize("name,shape", [("cfg2_f32_2048", None), ("cfg3_bf16_8192", (2048, 2048, 1024)),
+                                        ("cfg5_e4m3_16384", (1024, 2048, 1024))])
+def test_cublas_comparator(ctx, name, shape):
+    # pf_time_cublas: cublasLt GEMM alone and GEMM + separate bias/GELU on the bound operands; the unfused
+    # result it leaves in C agrees with the fused kernel within the dtype's tolerance.
+    w = wl.CONFIGS[name] if shape is None else wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w)
+    A, B, bias, C = device_operands(w, inp)
+    fused = run_pf(ctx, w, inp, None, (A, B, bias, C)).clone()
+    gemm_ms, unfused_ms = ctx.time_cublas(warmup=2, iters=5, reps=3)
+    assert 0 < gemm_ms < unfused_ms
+    torch.cuda.synchronize()
+    assert max_rel_err_t(fused.float(), C.float()) <= TOL[w.dtype]

@@ -57,7 +57,10 @@ def test_measure_ok_and_gated(tune_fake):
     rc, j, _ = measure(tune_fake, GOOD)
     assert rc == 0 and j["ok"] and j["gflops"] > 0
     assert j["profile"]["max_err"] < 2e-2
-    assert j["profile"]["regs"] == 149 and j["cublas_gflops"] is None
+    assert j["profile"]["regs"] == 149
+    # the fake's cuBLAS comparator reports 0.9 ms (GEMM alone) and 1.4 ms (GEMM + separate bias/GELU)
+    flops = 2.0 * 256 * 256 * 128
+    assert abs(j["cublas_gflops"] - flops / 0.9e6) < 1e-6 and abs(j["cublas_unfused_gflops"] - flops / 1.4e6) < 1e-6
 
 
 @pytest.mark.parametrize("gpus", [2, 3, 8])
