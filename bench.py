@@ -145,45 +145,6 @@ def Dist(n_gpus: int):
 
 
 # ------------------------------------------------------------------------------------------------
-class Dist:
-    def __init__(self, n_gpus: int):
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-        if self.world != n_gpus:
-            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}: launch N>1 with torchrun")
-        self.pg = None
-        if self.world > 1:
-            import datetime
-
-            import torch
-            import torch.distributed as dist
-            torch.cuda.set_device(self.local_rank)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                    device_id=torch.device("cuda", self.local_rank))
-            self.pg = dist
-
-    def barrier(self):
-        if self.pg:
-            import torch
-            self.pg.barrier(device_ids=[self.local_rank])
-            torch.cuda.synchronize()
-
-    def max(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
-        return float(t.item())
-
-    def close(self):
-        if self.pg:
-            self.pg.barrier(device_ids=[self.local_rank])
-            self.pg.destroy_process_group()
-
-
-# ------------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------------
 def device_operands(torch, w, inp, r0, rows):
