@@ -53,6 +53,14 @@ def parse_args():
     return ap.parse_args()
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (torchrun sets OMP_NUM_THREADS=1; the CPU legs ignore it)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -190,7 +198,7 @@ def gate_sampled(torch, A, B, bias, C, scale, tol, n=256, seed=1234):
 def cpu_baseline_sample(w, inp, seconds: float):
     """Time the oracle port of the CPU-lowered schedule on a bounded row sample, all host threads."""
     import oracle
-    threads = oracle.num_threads()
+    threads = host_threads()
     out = np.empty((w.M, w.N), dtype=np.float32)
     t0 = time.perf_counter()
     oracle.cpu_schedule(inp.A, inp.B, inp.bias, 64, 64, 16, row0=0, rows=2, threads=threads, out=out)
@@ -347,7 +355,7 @@ def run_reference(args, dist):
 
     w = wl.CONFIGS[args.config]
     inp = wl.make_inputs(w)
-    threads = oracle.num_threads()
+    threads = host_threads()
     out = np.empty((w.M, w.N), dtype=np.float32)
     t0 = time.perf_counter()
     oracle.cpu_schedule(inp.A, inp.B, inp.bias, 64, 64, 16, row0=0, rows=1, threads=threads, out=out)
