@@ -289,6 +289,10 @@ struct pf_ctx {
   size_t capA = 0, capB = 0, capC = 0, capBias = 0;
 
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+  // pf_run_host pipeline: compute and device-to-host streams, and per-chunk ordering events
+  cudaStream_t s_comp = nullptr, s_out = nullptr;
+  std::vector<cudaEvent_t> ev_pool;
 };
 
 namespace {
@@ -469,6 +473,9 @@ int pf_close(pf_ctx *c) {
     if (c->hbufBias) cudaFree(c->hbufBias);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
+    for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
+    if (c->s_comp) cudaStreamDestroy(c->s_comp);
+    if (c->s_out) cudaStreamDestroy(c->s_out);
     if (c->stream) cudaStreamDestroy(c->stream);
     if (c->module) driver_api().moduleUnload(c->module);
   }
@@ -721,9 +728,8 @@ int pf_device_status(pf_ctx *c, unsigned *err_word) {
 }  // extern "C"
 
 namespace {
-// Context-owned device operands sized for the prepared problem; async H2D copies on the context's
-// stream; bind.  Shared by pf_upload and pf_run_host.
-int stage_inputs(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
+// Context-owned device operands sized for the prepared problem, bound to the context.
+int ensure_host_bufs(pf_ctx *c, float sa, float sb) {
   const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
   const size_t nA = static_cast<size_t>(c->M) * c->K * e, nB = static_cast<size_t>(c->K) * c->N * e;
   const size_t nC = static_cast<size_t>(c->M) * c->N * o, nBias = static_cast<size_t>(c->N) * sizeof(float);
@@ -744,13 +750,64 @@ int stage_inputs(pf_ctx *c, const void *hA, const void *hB, const float *hbias, 
       (rc = ensure(&c->hbufC, &c->capC, nC)) ||
       (rc = ensure(reinterpret_cast<void **>(&c->hbufBias), &c->capBias, nBias)))
     return rc;
-  PF_CUDA(c, cudaMemcpyAsync(c->hbufA, hA, nA, cudaMemcpyHostToDevice, c->stream));
-  PF_CUDA(c, cudaMemcpyAsync(c->hbufB, hB, nB, cudaMemcpyHostToDevice, c->stream));
-  PF_CUDA(c, cudaMemcpyAsync(c->hbufBias, hbias, nBias, cudaMemcpyHostToDevice, c->stream));
   if (!c->bound || c->A != c->hbufA || c->B != c->hbufB || c->C != c->hbufC || c->bias != c->hbufBias ||
       c->sa != sa || c->sb != sb) {
     if ((rc = pf_bind(c, c->hbufA, c->hbufB, c->hbufBias, c->hbufC, sa, sb))) return rc;
   }
+  return PF_OK;
+}
+
+// Launch the bound problem restricted to output rows [r0, r0 + rows) on stream s: the same kernel
+// variant on row windows of A and C (TMA maps re-encoded for the window on the tensor path).
+int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
+  const Variant &v = c->var;
+  const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
+  const void *A = static_cast<const char *>(c->A) + static_cast<size_t>(r0) * c->K * e;
+  void *C = static_cast<char *>(c->C) + static_cast<size_t>(r0) * c->N * o;
+  if (v.path == Path::kTensor) {
+    const CUtensorMapDataType in_t =
+        (c->dtype == PF_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUtensorMap tmA, tmC;
+    int rc;
+    if ((rc = encode_2d(c, &tmA, in_t, A, c->K, rows, c->K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (rc = encode_2d(c, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, c->N, rows, c->N * 2ull, 64, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+    TcParams p;
+    p.bias = c->bias;
+    p.scale = c->sa * c->sb;
+    p.M = rows;
+    p.N = c->N;
+    p.K = c->K;
+    p.num_m_blocks = (rows + v.bm - 1) / v.bm;
+    p.num_n_blocks = (c->N + v.bn - 1) / v.bn;
+    p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+    p.k_blocks = (c->K + v.bk_elems - 1) / v.bk_elems;
+    p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
+    p.status = c->d_status;
+    p.timeout_ns = c->timeout_ns;
+    v.launch_tc(dim3(std::min(p.num_tiles, c->max_units) * v.cta_per_tile), s, tmA, c->tmB, tmC, p);
+  } else if (v.path == Path::kSimt) {
+    dim3 grid((c->N + v.sbn - 1) / v.sbn, (rows + v.sbm - 1) / v.sbm);
+    v.launch_simt(grid, s, static_cast<const float *>(A), static_cast<const float *>(c->B), c->bias,
+                  static_cast<float *>(C), rows, c->N, c->K, c->simt_vec);
+  } else {
+    return set_err(c, PF_ESTATE, "row-window launch on an image");
+  }
+  PF_CUDA(c, cudaGetLastError());
+  return PF_OK;
+}
+
+// Context-owned device operands sized for the prepared problem; async H2D copies on the context's
+// stream; bind.  Used by pf_upload.
+int stage_inputs(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
+  const size_t e = pf_elem_bytes(c->dtype);
+  int rc;
+  if ((rc = ensure_host_bufs(c, sa, sb))) return rc;
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufA, hA, static_cast<size_t>(c->M) * c->K * e, cudaMemcpyHostToDevice, c->stream));
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufB, hB, static_cast<size_t>(c->K) * c->N * e, cudaMemcpyHostToDevice, c->stream));
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufBias, hbias, static_cast<size_t>(c->N) * sizeof(float), cudaMemcpyHostToDevice,
+                             c->stream));
   return PF_OK;
 }
 }  // namespace
@@ -763,10 +820,45 @@ int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, v
   if (!hA || !hB || !hbias || !hC) return set_err(c, PF_EINVAL, "null host operand");
   DeviceGuard g(c->device);
   int rc;
-  if ((rc = stage_inputs(c, hA, hB, hbias, sa, sb))) return rc;
-  if ((rc = do_launch(c, c->stream))) return rc;
-  const size_t nC = static_cast<size_t>(c->M) * c->N * pf_out_bytes(c->dtype);
-  PF_CUDA(c, cudaMemcpyAsync(hC, c->hbufC, nC, cudaMemcpyDeviceToHost, c->stream));
+  if ((rc = ensure_host_bufs(c, sa, sb))) return rc;
+  const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
+  const size_t rowA = static_cast<size_t>(c->K) * e, rowC = static_cast<size_t>(c->N) * o;
+  // Row chunks (whole kernel tiles), at most 8: chunk i's GEMM starts as soon as B and its rows of A are
+  // in; its rows of C go back while later chunks are still arriving (copies in both directions and the
+  // kernels overlap).  An image keeps its fixed launch shape: one chunk.
+  const int align = c->var.path == Path::kTensor ? c->var.bm : c->var.path == Path::kSimt ? c->var.sbm : c->M;
+  const int units = (c->M + align - 1) / align;
+  const int P = c->var.path == Path::kImage ? 1 : std::max(1, std::min(8, units));
+  if (!c->s_comp) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_comp, cudaStreamNonBlocking));
+  if (!c->s_out) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
+  while (c->ev_pool.size() < static_cast<size_t>(2 * P + 1)) {
+    cudaEvent_t ev;
+    PF_CUDA(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    c->ev_pool.push_back(ev);
+  }
+  cudaEvent_t evB = c->ev_pool[0];
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufB, hB, static_cast<size_t>(c->K) * c->N * e, cudaMemcpyHostToDevice, c->stream));
+  PF_CUDA(c, cudaMemcpyAsync(c->hbufBias, hbias, static_cast<size_t>(c->N) * sizeof(float), cudaMemcpyHostToDevice,
+                             c->stream));
+  PF_CUDA(c, cudaEventRecord(evB, c->stream));
+  PF_CUDA(c, cudaStreamWaitEvent(c->s_comp, evB, 0));
+  for (int i = 0; i < P; ++i) {
+    const int r0 = static_cast<int>(static_cast<long long>(units) * i / P) * align;
+    const int r1 = std::min(c->M, static_cast<int>(static_cast<long long>(units) * (i + 1) / P) * align);
+    if (r1 <= r0) continue;
+    cudaEvent_t evA = c->ev_pool[1 + 2 * i], evC = c->ev_pool[2 + 2 * i];
+    PF_CUDA(c, cudaMemcpyAsync(static_cast<char *>(c->hbufA) + r0 * rowA, static_cast<const char *>(hA) + r0 * rowA,
+                               (r1 - r0) * rowA, cudaMemcpyHostToDevice, c->stream));
+    PF_CUDA(c, cudaEventRecord(evA, c->stream));
+    PF_CUDA(c, cudaStreamWaitEvent(c->s_comp, evA, 0));
+    if ((rc = P == 1 ? do_launch(c, c->s_comp) : launch_rows(c, c->s_comp, r0, r1 - r0))) return rc;
+    PF_CUDA(c, cudaEventRecord(evC, c->s_comp));
+    PF_CUDA(c, cudaStreamWaitEvent(c->s_out, evC, 0));
+    PF_CUDA(c, cudaMemcpyAsync(static_cast<char *>(hC) + r0 * rowC, static_cast<char *>(c->hbufC) + r0 * rowC,
+                               (r1 - r0) * rowC, cudaMemcpyDeviceToHost, c->s_out));
+  }
+  PF_CUDA(c, cudaStreamSynchronize(c->s_out));
+  PF_CUDA(c, cudaStreamSynchronize(c->s_comp));
   PF_CUDA(c, cudaStreamSynchronize(c->stream));
   return PF_OK;
 }

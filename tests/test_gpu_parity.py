@@ -293,3 +293,19 @@ def test_cublas_comparator(ctx, name, shape):
     assert 0 < gemm_ms < unfused_ms
     torch.cuda.synchronize()
     assert max_rel_err_t(fused.float(), C.float()) <= TOL[w.dtype]
+
+
+@pytest.mark.parametrize("name,shape,tile", [("cfg3_bf16_8192", (2048, 1024, 768), None),
+                                             ("cfg3_bf16_8192", (1000, 520, 264), (128, 256, 32, 4, 16, 0)),
+                                             ("cfg5_e4m3_16384", (1536, 512, 512), None),
+                                             ("cfg2_f32_2048", (1030, 256, 128), None)])
+def test_pipelined_host_path_equals_device_path(ctx, name, shape, tile):
+    # pf_run_host splits rows into chunks whose copies and kernels overlap; the result is the single launch's.
+    w = wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w, seed=17)
+    C = run_pf(ctx, w, inp, tile)
+    hC = np.empty((w.M, w.N), dtype=np.float32 if w.dtype == "f32" else np.uint16)
+    ctx.prepare(w.dtype, tile, w.M, w.N, w.K)
+    ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC, inp.scale_a, inp.scale_b)
+    want = C.cpu().numpy() if w.dtype == "f32" else C.view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.array_equal(hC, want)
