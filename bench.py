@@ -10,8 +10,10 @@ step time is the max over ranks of each rank's CUDA-event time (strong scaling: 
 fixed).  FLOPs are 2*M*N*K (the epilogue is not counted, as in the reference, space.hpp:55).
 
 Besides the device-timed `value`, the line carries
-  e2e           the same metric through the C ABI's host-buffer call (pf_run_host): H2D of A, B, bias
-                from pinned memory, the kernel, D2H of C, every step
+  e2e           the same metric end to end from pinned host buffers, every step: at N=1 the C ABI's
+                pf_run_host (H2D of A, B, bias, the kernel, D2H of C, overlapped in row chunks); at N>1
+                ptxforge_b200.sharded.ShardedHostGemm (each rank copies its A rows and 1/N of B, B is
+                all-gathered over NVLink, kernel on the local rows, D2H of its C rows)
   roofline      achieved TFLOP/s of the kernel over the measured dense bf16 peak
   comparators   cuBLAS GEMM alone and cuBLAS + a separate bias+GELU pass (pf_time_cublas), same inputs
   cpu_baseline  the CPU-lowered schedule (oracle port) on the host cores, on a bounded sample (N=1)
