@@ -30,7 +30,8 @@ OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
 SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
            "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
-           "pf_gemm_bias_gelu_noalloc", "pf_prepare_image", "pf_time_cublas")
+           "pf_gemm_bias_gelu_noalloc", "pf_prepare_image", "pf_time_cublas",
+           "pf_set_stream_k")
 
 
 class Tile(ctypes.Structure):
@@ -102,6 +103,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_prepare_image.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, i, i, i, i, i, i]
         dp = ctypes.POINTER(ctypes.c_double)
         lib.pf_time_cublas.argtypes = [vp, i, i, i, dp, dp]
+        lib.pf_set_stream_k.argtypes = [vp, i]
         lib.pf_gemm_bias_gelu_noalloc.argtypes = [i, i, ctypes.POINTER(Tile), i, i, i, vp, vp, vp, vp, ctypes.c_float,
                                                   ctypes.c_float, vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p,
                                                   ctypes.c_size_t]
@@ -114,7 +116,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
                      "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc",
-                     "pf_prepare_image", "pf_time_cublas"):
+                     "pf_prepare_image", "pf_time_cublas", "pf_set_stream_k"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -227,6 +229,10 @@ class Context:
         w = ctypes.c_uint()
         self._check(self._lib.pf_device_status(self._h, ctypes.byref(w)), "pf_device_status")
         return w.value
+
+    def set_stream_k(self, mode: int):
+        """Stream-K tail of the CTA-pair kernel: -1 auto (default), 0 off, 1 on (pf_set_stream_k)."""
+        self._check(self._lib.pf_set_stream_k(self._h, mode), "pf_set_stream_k")
 
     def set_wait_timeout(self, ns: int):
         self._check(self._lib.pf_set_wait_timeout(self._h, ns), "pf_set_wait_timeout")

@@ -38,6 +38,13 @@ struct TcParams {
   int group_m;             // raster: tiles walk `group_m` M-blocks before moving to the next N-block
   unsigned *status;        // device status word (bounded-wait timeouts)
   unsigned long long timeout_ns;
+  // Stream-K tail (CTA-pair kernel only; dp_tiles == num_tiles turns it off): tiles [0, dp_tiles) are
+  // processed whole; the k-iterations of tiles [dp_tiles, num_tiles) are spread evenly over the workers.
+  int dp_tiles = 0;
+  long long sk_iters = 0;  // (num_tiles - dp_tiles) * k_blocks
+  unsigned epoch = 0;      // this launch's tag for the partial-ready flags
+  float *sk_partials = nullptr;    // [workers][2 CTAs][128 x 256] fp32
+  unsigned *sk_flags = nullptr;    // [workers][2 CTAs]
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).
@@ -104,14 +111,19 @@ enum : unsigned {
   kErrTeardownWait = 8u,
 };
 
+struct NoAddend {
+  __device__ __forceinline__ void operator()(uint32_t (&)[32], int) const {}
+};
+
 // One epilogue warp turns its 32 accumulator rows x BN columns (TMEM lanes q*32.., columns from
 // `t_row`) into C rows [m0, m0+32) x columns [n_tile, n_tile+BN): x*scale + bias[c], GELU, bf16,
 // staged through a double-buffered 32 x 64 swizzled shared-memory box and TMA-stored.
-// `release()` is called by the whole warp right after the last TMEM load of the tile.
-template <int BN, class Release>
+// `release()` is called by the whole warp right after the last TMEM load of the tile; `addend(v, c0)`
+// may add other fp32 contributions to accumulator columns [c0, c0+32) before the epilogue math.
+template <int BN, class Release, class Addend = NoAddend>
 __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile, const TcParams &p,
                                               const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
-                                              Release release) {
+                                              Release release, Addend addend = Addend()) {
   constexpr int EPI_COLS = 64;
   constexpr int BUF_BYTES = 32 * EPI_COLS * 2;
 #pragma unroll 1
@@ -122,6 +134,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c * EPI_COLS + h * 32, v);
       tmem_ld_wait();
+      addend(v, c * EPI_COLS + h * 32);
       const int n0 = n_tile + c * EPI_COLS + h * 32;
       uint32_t packed[16];
 #pragma unroll

@@ -10,8 +10,17 @@
 //     accumulator rows x 256 columns;
 //   * tcgen05.commit multicasts the stage-free and accumulator-ready signals to both CTAs;
 //   * each CTA's four epilogue warps drain its own TMEM rows and signal the leader's `tempty`.
-// Per SM this halves the shared-memory B traffic of the 1-CTA 128 x 256 kernel and, at 32 KB per
-// stage, leaves room for 6 pipeline stages.
+// Per SM this halves the shared-memory B traffic of the 1-CTA 128 x 256 kernel; at 32 KB per k-atom
+// and stage, 3 stages of two k-atoms (or 6 of one) fit.
+//
+// Work units.  A pair ("worker") walks a list of units that all three roles enumerate identically
+// (sk_unit): first whole tiles, round-robin over the workers (data-parallel), then, when the launch
+// enables the stream-K tail (p.sk_iters > 0), a contiguous share of the k-iterations of the last
+// tiles, so a partial last wave does not leave SMs idle.  A tail tile is split between consecutive
+// workers: the one holding the tile's first k-block ("head") finishes it; the others ("partials")
+// write their fp32 accumulators to a workspace and raise a flag tagged with the launch's epoch; the
+// head adds them in its epilogue.  A worker's partial is its first tail unit and its head its last,
+// so heads rarely wait; every wait is bounded.
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -41,14 +50,67 @@ struct Tc2Config {
   static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1 + 1;
   static constexpr int TMEM_COLS = 512;                      // 2 accumulators x 256 columns
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 192;
+  static constexpr int PARTIAL_FLOATS = BM_CTA * BN;         // one CTA's share of a tile, fp32
   static constexpr uint32_t IDESC =
       instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ 256);
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
 };
+
+enum : int { kUnitWhole = 0, kUnitHead = 1, kUnitPartial = 2 };
+
+struct SkUnit {
+  int tile;      // global tile index (tile_coords order)
+  int kb0, kb1;  // k-block range [kb0, kb1)
+  int kind;      // kUnitWhole / kUnitHead / kUnitPartial
+};
+
+// Unit `u` of worker `w` of `W`; false past the worker's last unit.
+__device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, SkUnit &out) {
+  const int dp = p.sk_iters > 0 ? p.dp_tiles : p.num_tiles;
+  const int n_dp = w < dp ? (dp - 1 - w) / W + 1 : 0;
+  if (u < n_dp) {
+    out = {w + u * W, 0, p.k_blocks, kUnitWhole};
+    return true;
+  }
+  if (p.sk_iters <= 0) return false;
+  u -= n_dp;
+  const long long KB = p.k_blocks;
+  const long long s = static_cast<long long>(w) * p.sk_iters / W;
+  const long long e = static_cast<long long>(w + 1) * p.sk_iters / W;
+  long long pos = s;
+  for (int i = 0; pos < e; ++i) {
+    const long long local = pos / KB;
+    const long long seg_end = min(e, (local + 1) * KB);
+    if (i == u) {
+      out.tile = dp + static_cast<int>(local);
+      out.kb0 = static_cast<int>(pos - local * KB);
+      out.kb1 = static_cast<int>(seg_end - local * KB);
+      out.kind = out.kb0 == 0 ? (out.kb1 == KB ? kUnitWhole : kUnitHead) : kUnitPartial;
+      return true;
+    }
+    pos = seg_end;
+  }
+  return false;
+}
+
+// First k-iteration (in the tail's linear k space) owned by worker w.
+__device__ __forceinline__ long long sk_start(int w, int W, const TcParams &p) {
+  return static_cast<long long>(w) * p.sk_iters / W;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 template <class Cfg>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
@@ -67,7 +129,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [2] both: accumulator ready
   uint64_t *tempty = tfull + 2;                 // [2] leader: both CTAs drained the accumulator
   uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *epi_sync = drain + 1;               // [1] the 4 epilogue warps wrote this worker's partial
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_sync + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,6 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       mbar_init(&tempty[a], 2 * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(epi_sync, Cfg::EPI_WARPS);        // completes at most once: a worker has at most one partial
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -115,12 +179,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int issued = 0;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      SkUnit un;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
         int mb, nb;
-        tile_coords(t, p, mb, nb);
+        tile_coords(un.tile, p, mb, nb);
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
@@ -160,7 +225,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      SkUnit un;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
           ok = false;
@@ -168,7 +234,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
@@ -183,10 +249,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             const uint64_t ad =
                 smem_desc(a_addr + (k / PER_ATOM) * Cfg::A_ATOM_BYTES + (k % PER_ATOM) * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+            const uint32_t accumulate = (kb != un.kb0 || k != 0) ? 1u : 0u;
             if constexpr (Cfg::ELEM == 2)
-              tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+              tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, accumulate);
             else
-              tc_mma_f8_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+              tc_mma_f8_pair(d_tmem, ad, bd, Cfg::IDESC, accumulate);
           }
           tc_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == Cfg::STAGES) {
@@ -213,9 +280,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int buf = 0;
-    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+    SkUnit un;
+    // This CTA's partial-sum slot (its 128 rows of a tile) in worker `w`'s workspace; a warp's 32 rows
+    // are stored quad-of-columns-major so one warp-wide 16-byte access covers 512 contiguous bytes.
+    auto slot = [&](int w) -> float4 * {
+      return reinterpret_cast<float4 *>(p.sk_partials + (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
+                                        static_cast<size_t>(q) * 32 * Cfg::BN);
+    };
+    for (int u = 0; sk_unit(pair, num_pairs, u, p, un); ++u) {
       int mb, nb;
-      tile_coords(t, p, mb, nb);
+      tile_coords(un.tile, p, mb, nb);
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
@@ -225,9 +299,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
       const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[acc]), 0);
-      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, ebuf, buf, lane, [&] {
+      if (un.kind == kUnitPartial) {
+        // Write this worker's fp32 partial (its k-range of the tile) and raise its flag.
+        float4 *dst = slot(pair);
+#pragma unroll 1
+        for (int c = 0; c < Cfg::BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            __stcg(dst + (c * 8 + j4) * 32 + lane,
+                   make_float4(__uint_as_float(v[j4 * 4 + 0]), __uint_as_float(v[j4 * 4 + 1]),
+                               __uint_as_float(v[j4 * 4 + 2]), __uint_as_float(v[j4 * 4 + 3])));
+        }
+        tc_fence_before();
+        __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      });
+        // Every warp's stores are visible device-wide before it arrives; one lane publishes the flag
+        // once all four have arrived (bounded wait, never a hardware barrier a departed warp could block).
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_sync);
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait(epi_sync, 0, p.timeout_ns, abort_flag))
+            st_release_gpu(p.sk_flags + pair * 2 + rank, p.epoch);
+          else
+            fail(kErrEpilogueWait);
+        }
+      } else {
+        // Whole tile, or the head of a tail tile: add the later workers' partials (bounded waits).
+        int first = 0, last = -1;
+        if (un.kind == kUnitHead) {
+          const long long tile_end = static_cast<long long>(un.tile - p.dp_tiles + 1) * p.k_blocks;
+          first = pair + 1;
+          last = pair;
+          while (last + 1 < num_pairs && sk_start(last + 1, num_pairs, p) < tile_end) ++last;
+          bool ok = true;
+          if (lane == 0) {
+            for (int w = first; w <= last && ok; ++w) {
+              const unsigned *flag = p.sk_flags + w * 2 + rank;
+              if (ld_acquire_gpu(flag) != p.epoch) {
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_gpu(flag) != p.epoch) {
+                  if (*abort_flag || globaltimer_ns() - t0 > p.timeout_ns) {
+                    ok = false;
+                    break;
+                  }
+                  __nanosleep(256);
+                }
+              }
+            }
+            if (!ok) fail(kErrEpilogueWait);
+          }
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        }
+        auto addend = [&](uint32_t(&v)[32], int c0) {
+          for (int w = first; w <= last; ++w) {
+            const float4 *src = slot(w) + (c0 / 4) * 32 + lane;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 s = __ldcg(src + j4 * 32);
+              v[j4 * 4 + 0] = __float_as_uint(__uint_as_float(v[j4 * 4 + 0]) + s.x);
+              v[j4 * 4 + 1] = __float_as_uint(__uint_as_float(v[j4 * 4 + 1]) + s.y);
+              v[j4 * 4 + 2] = __float_as_uint(__uint_as_float(v[j4 * 4 + 2]) + s.z);
+              v[j4 * 4 + 3] = __float_as_uint(__uint_as_float(v[j4 * 4 + 3]) + s.w);
+            }
+          }
+        };
+        epilogue_rows<Cfg::BN>(
+            t_row, m0, nb * Cfg::BN, p, &tmC, ebuf, buf, lane,
+            [&] {
+              if (lane == 0) mbar_arrive_cluster(tempty_leader);
+            },
+            addend);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;

@@ -290,6 +290,13 @@ struct pf_ctx {
 
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
+  // stream-K tail of the CTA-pair kernel: mode (-1 auto, 0 off, 1 on), launch epoch, workspace, flags
+  int stream_k = -1;
+  unsigned epoch = 0;
+  float *sk_ws = nullptr;
+  unsigned *sk_flags = nullptr;
+  size_t sk_ws_cap = 0, sk_flags_cap = 0;
+
   // pf_run_host pipeline: compute and device-to-host streams, and per-chunk ordering events
   cudaStream_t s_comp = nullptr, s_out = nullptr;
   std::vector<cudaEvent_t> ev_pool;
@@ -362,6 +369,50 @@ int encode_maps(pf_ctx *c) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Tiles of the stream-K tail for a CTA-pair launch of `tiles` tiles (0 = pure data-parallel).  With
+// W resident pairs the tail is the partial last wave, R = tiles mod W (all tiles if fewer than W), so a
+// pair's share of the tail is below one tile.  Auto mode uses it when the partial wave would waste
+// more than 3 % of the launch.
+int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
+  if (c->var.cta_per_tile != 2 || c->stream_k == 0) return 0;
+  const int W = c->max_units;
+  const int R = tiles % W;
+  if (R == 0 || static_cast<long long>(R) * k_blocks < W) return 0;
+  if (c->stream_k < 0) {
+    const double waves = static_cast<double>(tiles) / W;
+    if (std::ceil(waves) / waves < 1.03) return 0;
+  }
+  return R;
+}
+
+int ensure_sk_workspace(pf_ctx *c, int workers) {
+  const size_t ws = static_cast<size_t>(workers) * 2 * 128 * 256 * sizeof(float);
+  const size_t fl = static_cast<size_t>(workers) * 2 * sizeof(unsigned);
+  if (c->sk_ws_cap < ws) {
+    if (c->sk_ws) cudaFree(c->sk_ws);
+    c->sk_ws = nullptr;
+    c->sk_ws_cap = 0;
+    if (cudaMalloc(&c->sk_ws, ws) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, PF_ENOMEM, "cudaMalloc(%zu) for the stream-K workspace failed", ws);
+    }
+    c->sk_ws_cap = ws;
+  }
+  if (c->sk_flags_cap < fl) {
+    if (c->sk_flags) cudaFree(c->sk_flags);
+    c->sk_flags = nullptr;
+    c->sk_flags_cap = 0;
+    if (cudaMalloc(&c->sk_flags, fl) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, PF_ENOMEM, "cudaMalloc(%zu) for the stream-K flags failed", fl);
+    }
+    PF_CUDA(c, cudaMemset(c->sk_flags, 0, fl));  // epochs start at 1: no flag is set
+    c->sk_flags_cap = fl;
+    c->epoch = 0;
+  }
+  return PF_OK;
+}
+
 int do_launch(pf_ctx *c, cudaStream_t s) {
   if (!c->prepared) return set_err(c, PF_ESTATE, "pf_launch before pf_prepare");
   if (!c->bound) return set_err(c, PF_ESTATE, "pf_launch before pf_bind");
@@ -380,7 +431,22 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
-    dim3 grid(std::min(p.num_tiles, c->max_units) * v.cta_per_tile);
+    int workers = std::min(p.num_tiles, c->max_units);
+    const int sk_tiles = sk_tail_tiles(c, p.num_tiles, p.k_blocks);
+    if (sk_tiles > 0) {
+      // Stream-K tail: whole waves stay data-parallel, the last sk_tiles tiles' k-iterations are
+      // shared by every resident pair.  Workspace: one 256 KB partial per pair (two CTAs x 128 x 256 fp32).
+      workers = c->max_units;
+      int rc;
+      if ((rc = ensure_sk_workspace(c, workers))) return rc;
+      if (++c->epoch == 0) c->epoch = 1;
+      p.dp_tiles = p.num_tiles - sk_tiles;
+      p.sk_iters = static_cast<long long>(sk_tiles) * p.k_blocks;
+      p.epoch = c->epoch;
+      p.sk_partials = c->sk_ws;
+      p.sk_flags = c->sk_flags;
+    }
+    dim3 grid(workers * v.cta_per_tile);
     v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, p);
   } else if (v.path == Path::kImage) {
     // The reference's parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} (cuda_runner.cpp:182).
@@ -466,6 +532,8 @@ int pf_close(pf_ctx *c) {
     DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     cublas_cmp_release(c);
+    if (c->sk_ws) cudaFree(c->sk_ws);
+    if (c->sk_flags) cudaFree(c->sk_flags);
     if (c->d_status) cudaFree(c->d_status);
     if (c->hbufA) cudaFree(c->hbufA);
     if (c->hbufB) cudaFree(c->hbufB);
@@ -531,6 +599,12 @@ int pf_prepare_image(pf_ctx *c, const void *image, size_t image_bytes, const cha
 }
 
 const char *pf_last_error(const pf_ctx *c) { return c ? c->err.c_str() : "null context"; }
+
+int pf_set_stream_k(pf_ctx *c, int mode) {
+  if (!c || mode < -1 || mode > 1) return set_err(c, PF_EINVAL, "stream-K mode must be -1, 0 or 1");
+  c->stream_k = mode;
+  return PF_OK;
+}
 
 int pf_set_wait_timeout(pf_ctx *c, unsigned long long ns) {
   if (!c || ns == 0) return set_err(c, PF_EINVAL, "timeout must be positive");
@@ -709,7 +783,9 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
   out->num_sms = c->num_sms;
   if (c->var.path == Path::kTensor) {
     const int tiles = ((c->M + c->var.bm - 1) / c->var.bm) * ((c->N + c->var.bn - 1) / c->var.bn);
-    out->grid = std::min(tiles, c->max_units) * c->var.cta_per_tile;
+    const int kb = (c->K + c->var.bk_elems - 1) / c->var.bk_elems;
+    const int workers = sk_tail_tiles(c, tiles, kb) > 0 ? c->max_units : std::min(tiles, c->max_units);
+    out->grid = workers * c->var.cta_per_tile;
   } else {
     out->grid = ((c->N + c->var.sbn - 1) / c->var.sbn) * ((c->M + c->var.sbm - 1) / c->var.sbm);
   }

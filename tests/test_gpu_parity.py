@@ -194,10 +194,12 @@ def test_full_size_gate_torch_and_determinism(ctx, oracle_mod, name):
 @pytest.mark.parametrize("G", [2, 3, 8])
 def test_row_shards_equal_unsharded(ctx, pf, G):
     # Row sharding (the multi-GPU decomposition) on one GPU: each shard is its own launch on a row
-    # window of A and C; the concatenation is bit-identical to the single launch.
+    # window of A and C; the concatenation is bit-identical to the single launch (every tile whole:
+    # stream-K off, since the tail's split depends on the launch shape).
     w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 2048, 1024, 768)
     inp = wl.make_inputs(w, seed=9)
     A, B, bias, C = device_operands(w, inp)
+    ctx.set_stream_k(0)
     run_pf(ctx, w, inp, None, (A, B, bias, C))
     Cs = torch.full_like(C, float("nan"))
     for g in range(G):
@@ -209,6 +211,7 @@ def test_row_shards_equal_unsharded(ctx, pf, G):
         ctx.launch(torch.cuda.current_stream())
     torch.cuda.synchronize()
     assert ctx.status() == 0
+    ctx.set_stream_k(-1)
     assert torch.equal(C, Cs)
 
 
@@ -225,6 +228,7 @@ def test_run_host_equals_device_path(ctx, pf):
 def test_timing_protocol_and_attrs(ctx):
     w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 1024, 1024, 1024)
     inp = wl.make_inputs(w)
+    ctx.set_stream_k(0)  # whole tiles: the grid is min(resident CTAs or pairs, tiles)
     for tile, tiles, per_tile in (((128, 256, 32, 4, 16, 0), (1024 // 128) * (1024 // 256), 1),
                                   ((256, 256, 32, 8, 8, 1), (1024 // 256) * (1024 // 256), 2)):
         run_pf(ctx, w, inp, tile)
@@ -234,6 +238,7 @@ def test_timing_protocol_and_attrs(ctx):
         # local_bytes is the per-thread stack frame (8 B of bookkeeping); ptxas reports 0 bytes of spills
         assert a["threads"] == 192 and a["blocks_per_sm"] == 1 and a["local_bytes"] <= 16
         assert a["num_sms"] == 148 and a["grid"] == min(a["num_sms"] // per_tile, tiles) * per_tile
+    ctx.set_stream_k(-1)
 
 
 def test_invalid_configs_are_errors(ctx, pf):
@@ -300,12 +305,60 @@ def test_cublas_comparator(ctx, name, shape):
                                              ("cfg5_e4m3_16384", (1536, 512, 512), None),
                                              ("cfg2_f32_2048", (1030, 256, 128), None)])
 def test_pipelined_host_path_equals_device_path(ctx, name, shape, tile):
-    # pf_run_host splits rows into chunks whose copies and kernels overlap; the result is the single launch's.
+    # pf_run_host splits rows into chunks whose copies and kernels overlap; the result is the single launch's
+    # (stream-K off on the single launch: the chunks run every tile whole).
     w = wl.scaled(wl.CONFIGS[name], *shape)
     inp = wl.make_inputs(w, seed=17)
+    ctx.set_stream_k(0)
     C = run_pf(ctx, w, inp, tile)
+    ctx.set_stream_k(-1)
     hC = np.empty((w.M, w.N), dtype=np.float32 if w.dtype == "f32" else np.uint16)
     ctx.prepare(w.dtype, tile, w.M, w.N, w.K)
     ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC, inp.scale_a, inp.scale_b)
     want = C.cpu().numpy() if w.dtype == "f32" else C.view(torch.int16).cpu().numpy().view(np.uint16)
     assert np.array_equal(hC, want)
+
+
+# ---------------------------------------------------------------------------------------------
+# stream-K tail of the CTA-pair kernel
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (512, 2048, 4096)),    # 16 tiles < 74 pairs
+                                        ("cfg3_bf16_8192", (1024, 8192, 2048)),   # 128 tiles: 1.73 waves
+                                        ("cfg3_bf16_8192", (600, 1000, 1000)),    # ragged edges, K tail
+                                        ("cfg5_e4m3_16384", (1024, 4096, 2048))])
+def test_stream_k_tail_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape):
+    w = wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w, seed=31)
+    ops = device_operands(w, inp)
+    A, B, bias, C = ops
+    ctx.set_stream_k(1)
+    try:
+        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), ops)
+        a = ctx.attrs()
+        assert a["grid"] == 148  # the tail spreads over every resident pair
+        ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias, inp.scale_a * inp.scale_b)
+        err = oracle_mod.max_rel_err(ref, to_np(C))
+        assert err <= TOL[w.dtype], f"stream-K: {err:.3e}"
+        C2 = torch.full_like(C, float("nan"))
+        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), (A, B, bias, C2))
+        assert torch.equal(C, C2)  # deterministic for a given shape
+        ctx.set_stream_k(0)
+        C3 = torch.full_like(C, float("nan"))
+        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), (A, B, bias, C3))
+        assert max_rel_err_t(C3.float(), C.float()) <= TOL[w.dtype]
+    finally:
+        ctx.set_stream_k(-1)
+
+
+def test_stream_k_forced_at_full_size(ctx, oracle_mod):
+    w = wl.CONFIGS["cfg3_bf16_8192"]
+    inp = wl.make_inputs(w)
+    A, B, bias, C = device_operands(w, inp)
+    ctx.set_stream_k(1)
+    try:
+        run_pf(ctx, w, inp, None, (A, B, bias, C))
+    finally:
+        ctx.set_stream_k(-1)
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= 2e-2
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= 2e-2
