@@ -371,8 +371,10 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Tiles of the stream-K tail for a CTA-pair launch of `tiles` tiles (0 = pure data-parallel).  With
 // W resident pairs the tail is the partial last wave, R = tiles mod W (all tiles if fewer than W), so a
-// pair's share of the tail is below one tile.  Auto mode uses it when the partial wave would waste
-// more than 3 % of the launch.
+// pair's share of the tail is below one tile.  Auto mode uses it only where it measured faster on B200:
+// at least 3 waves and a partial wave wasting more than 3 % (8192 x 8192 x 2048-row shards: 196 -> 194
+// us).  Below 2 waves the per-pair fixed costs (pipeline fill, the head's wait and partial reads, the
+// last epilogue) outweigh the rebalancing (1024-row shards: 105 -> 111 us), so auto stays data-parallel.
 int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
   if (c->var.cta_per_tile != 2 || c->stream_k == 0) return 0;
   const int W = c->max_units;
@@ -380,7 +382,7 @@ int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
   if (R == 0 || static_cast<long long>(R) * k_blocks < W) return 0;
   if (c->stream_k < 0) {
     const double waves = static_cast<double>(tiles) / W;
-    if (std::ceil(waves) / waves < 1.03) return 0;
+    if (waves < 3.0 || std::ceil(waves) / waves < 1.03) return 0;
   }
   return R;
 }
