@@ -17,6 +17,8 @@
 //      GPU at once behind a barrier; the trial's time is the max over GPUs;
 //   6. fills Measurement{ok, gflops, ms, profile{regs, local_bytes, static_smem, blocks_per_sm,
 //      occupancy, max_err}, error} (runner.hpp:20-25).
+// measure_many() runs up to Options::fanout such trials at once, each on its own group of GPUs; the
+// batched search that feeds it is tune_fanout() (ptxforge_b200/tune_fanout.hpp).
 #pragma once
 
 #include <algorithm>
@@ -76,12 +78,18 @@ class B200Runner : public Runner {
     // cuBLAS comparator once per problem (cuda_runner.hpp:28 `cublas`, cuda_runner.cpp:132-149):
     // Measurement.cublas_gflops = cuBLAS GEMM alone; cuBLAS + separate bias/GELU via cublas_unfused_gflops().
     bool cublas = true;
+    // Trial slots for measure_many(): slot s owns devices [device + s*gpus, device + (s+1)*gpus), so up
+    // to `fanout` candidate configs are gated and timed at once, each on its own GPU(s).  measure() uses
+    // slot 0 only.
+    int fanout = 1;
   };
 
   explicit B200Runner(Options o) : opt_(std::move(o)) {
     if (opt_.gpus < 1) throw std::runtime_error("B200Runner: gpus must be >= 1");
+    if (opt_.fanout < 1) throw std::runtime_error("B200Runner: fanout must be >= 1");
     if (opt_.tolerance <= 0) opt_.tolerance = pf_default_tolerance(opt_.dtype);
-    for (int g = 0; g < opt_.gpus; ++g) {
+    hC_.resize(static_cast<size_t>(opt_.fanout));
+    for (int g = 0; g < opt_.gpus * opt_.fanout; ++g) {
       pf_ctx *c = nullptr;
       int rc = pf_open(opt_.device + g, &c);
       if (rc) {
@@ -113,11 +121,57 @@ class B200Runner : public Runner {
   }
 
   Measurement measure(const Config &cfg, const Problem &p, const GPU &) override {
-    Measurement m;
     try {
       ensure(p);
+    } catch (const std::exception &ex) {
+      Measurement m;
+      m.error = ex.what();
+      return m;
+    }
+    return measure_on(0, cfg, p);
+  }
+
+  // Gate and time several configs at once, one per trial slot (Options::fanout); results come back in
+  // the order of `cfgs`.  With fanout 1 this is measure() on each config in turn.  Trials that share a
+  // batch run on different GPUs of the box at the same time; each is timed on its own GPU(s) only.
+  std::vector<Measurement> measure_many(const std::vector<Config> &cfgs, const Problem &p, const GPU &hw) {
+    std::vector<Measurement> out(cfgs.size());
+    if (opt_.fanout == 1) {
+      for (size_t i = 0; i < cfgs.size(); ++i) out[i] = measure(cfgs[i], p, hw);
+      return out;
+    }
+    try {
+      ensure(p);  // host inputs are generated once, then only read by the slots
+    } catch (const std::exception &ex) {
+      for (auto &m : out) m.error = ex.what();
+      return out;
+    }
+    for (size_t b = 0; b < cfgs.size(); b += static_cast<size_t>(opt_.fanout)) {
+      const int n = static_cast<int>(std::min(cfgs.size() - b, static_cast<size_t>(opt_.fanout)));
+      std::vector<std::thread> th;
+      th.reserve(static_cast<size_t>(n));
+      for (int s = 0; s < n; ++s) th.emplace_back([&, s] { out[b + s] = measure_on(s, cfgs[b + s], p); });
+      for (auto &t : th) t.join();
+    }
+    // the comparator is measured once per problem, by the first slot to pass; every passing trial reports it
+    for (auto &m : out)
+      if (m.ok) m.cublas_gflops = cublas_gflops_;
+    return out;
+  }
+
+  int fanout() const { return opt_.fanout; }
+
+ private:
+  // One trial on the contexts of trial slot `slot` (ctx_[slot*gpus .. slot*gpus + gpus)); ensure(p) has run.
+  Measurement measure_on(int slot, const Config &cfg, const Problem &p) {
+    Measurement m;
+    try {
       const pf_tile tile = to_tile(cfg);
-      const int G = static_cast<int>(ctx_.size());
+      const int G = opt_.gpus;
+      pf_ctx *const *cx = ctx_.data() + static_cast<size_t>(slot) * G;
+      std::vector<uint8_t> &hc = hC_[static_cast<size_t>(slot)];
+      hc.resize(static_cast<size_t>(p.M) * p.N * pf_out_bytes(opt_.dtype));
+      const int device0 = opt_.device + slot * G;
       const size_t e = pf_elem_bytes(opt_.dtype), o = pf_out_bytes(opt_.dtype);
       std::vector<int> row0(G), rows(G), rc(G, PF_OK);
       std::vector<std::string> err(G);
@@ -130,11 +184,11 @@ class B200Runner : public Runner {
       // prepare + upload + one gated launch per shard, each on its own host thread
       auto fail = [&](int g, int code) {
         rc[g] = code;
-        err[g] = pf_last_error(ctx_[g]);
+        err[g] = pf_last_error(cx[g]);
       };
       run_shards(G, [&](int g) {
         if (rows[g] == 0) return;
-        pf_ctx *c = ctx_[g];
+        pf_ctx *c = cx[g];
         int r = pf_prepare(c, opt_.dtype, &tile, rows[g], p.N, p.K);
         if (r == PF_ETILE && opt_.dtype == PF_F32 && opt_.jit) {
           std::string jerr;
@@ -151,7 +205,7 @@ class B200Runner : public Runner {
           return fail(g, r);
         if ((r = pf_attrs(c, &attr[g]))) return fail(g, r);
         if ((r = pf_launch(c, nullptr))) return fail(g, r);
-        if ((r = pf_download(c, hC_.data() + static_cast<size_t>(row0[g]) * p.N * o))) return fail(g, r);
+        if ((r = pf_download(c, hc.data() + static_cast<size_t>(row0[g]) * p.N * o))) return fail(g, r);
         unsigned st = 0;
         if ((r = pf_device_status(c, &st))) return fail(g, r);
         if (st) {
@@ -161,7 +215,7 @@ class B200Runner : public Runner {
       });
       for (int g = 0; g < G; ++g)
         if (rc[g]) {
-          m.error = (G > 1 ? "gpu " + std::to_string(opt_.device + g) + ": " : std::string()) + err[g];
+          m.error = (G > 1 ? "gpu " + std::to_string(device0 + g) + ": " : std::string()) + err[g];
           return m;
         }
       const pf_attr &a0 = attr[first_nonempty(rows)];
@@ -172,7 +226,7 @@ class B200Runner : public Runner {
       m.profile.occupancy = std::round(1e4 * a0.blocks_per_sm * a0.threads / 2048.0) / 1e4;
 
       // correctness gate first: never report speed for a wrong kernel
-      const double max_err = gate(p);
+      const double max_err = gate(p, hc);
       m.profile.max_err = max_err;
       if (!(max_err < opt_.tolerance)) {
         m.error = "incorrect result (max_err=" + std::to_string(max_err) + ", tolerance " +
@@ -185,7 +239,7 @@ class B200Runner : public Runner {
       run_shards(G, [&](int g) {
         sync.arrive_and_wait();
         if (rows[g] == 0) return;
-        int r = pf_time(ctx_[g], opt_.warmup, opt_.iters, opt_.reps, &ms[g]);
+        int r = pf_time(cx[g], opt_.warmup, opt_.iters, opt_.reps, &ms[g]);
         if (r) fail(g, r);
       });
       for (int g = 0; g < G; ++g)
@@ -199,7 +253,9 @@ class B200Runner : public Runner {
       m.gflops = p.flops() / (t * 1e6);
 
       // cuBLAS comparator, once per problem, on the same shards at once (failures leave it unset, as
-      // the reference's measure_cublas does when cuBLAS cannot be created)
+      // the reference's measure_cublas does when cuBLAS cannot be created); the first trial slot to pass
+      // measures it while the others wait
+      std::unique_lock<std::mutex> cmp_lock(cmp_mutex_);
       if (opt_.cublas && !cublas_gflops_) {
         std::vector<double> g_ms(G, 0.0), u_ms(G, 0.0);
         std::vector<int> crc(G, PF_OK);
@@ -207,7 +263,7 @@ class B200Runner : public Runner {
         run_shards(G, [&](int g) {
           sync2.arrive_and_wait();
           if (rows[g] == 0) return;
-          crc[g] = pf_time_cublas(ctx_[g], opt_.warmup, opt_.iters, opt_.reps, &g_ms[g], &u_ms[g]);
+          crc[g] = pf_time_cublas(cx[g], opt_.warmup, opt_.iters, opt_.reps, &g_ms[g], &u_ms[g]);
         });
         if (std::all_of(crc.begin(), crc.end(), [](int r) { return r == PF_OK; })) {
           cublas_gflops_ = p.flops() / (*std::max_element(g_ms.begin(), g_ms.end()) * 1e6);
@@ -222,6 +278,7 @@ class B200Runner : public Runner {
     return m;
   }
 
+ public:
   std::vector<Stage> stages(const Config &c, const Problem &, const GPU &) override {
     // Source only.  Compiler-written PTX/SASS of this build is never embedded in a trace.
     const std::string dir = opt_.root + "/ptxforge_b200/csrc/";
@@ -380,7 +437,6 @@ class B200Runner : public Runner {
     hbias_ = vbias_;
     hA_.assign(nA * e, 0);
     hB_.assign(nB * e, 0);
-    hC_.assign(static_cast<size_t>(p.M) * p.N * o, 0);
     vA_.resize(nA);
     vB_.resize(nB);
     sa_ = sb_ = 1.f;
@@ -421,7 +477,7 @@ class B200Runner : public Runner {
 
   // The reference gate (cuda_runner.cpp:189-197) over the gathered C.  A NaN at a sampled position
   // fails the trial.
-  double gate(const Problem &p) const {
+  double gate(const Problem &p, const std::vector<uint8_t> &hc) const {
     const size_t o = pf_out_bytes(opt_.dtype);
     const double scale = static_cast<double>(sa_) * sb_;
     std::mt19937 pick(99);
@@ -437,10 +493,10 @@ class B200Runner : public Runner {
       const size_t idx = static_cast<size_t>(r) * p.N + c;
       float got;
       if (o == 4) {
-        std::memcpy(&got, hC_.data() + idx * 4, 4);
+        std::memcpy(&got, hc.data() + idx * 4, 4);
       } else {
         uint16_t h;
-        std::memcpy(&h, hC_.data() + idx * 2, 2);
+        std::memcpy(&h, hc.data() + idx * 2, 2);
         const uint32_t u = static_cast<uint32_t>(h) << 16;
         std::memcpy(&got, &u, 4);
       }
@@ -454,10 +510,11 @@ class B200Runner : public Runner {
   Options opt_;
   std::vector<pf_ctx *> ctx_;
   Problem prob_{0, 0, 0};
-  std::vector<uint8_t> hA_, hB_, hC_;
+  std::vector<uint8_t> hA_, hB_;
+  std::vector<std::vector<uint8_t>> hC_;  // C on the host, one per trial slot
   std::vector<float> hbias_, vbias_, vA_, vB_;
   float sa_ = 1.f, sb_ = 1.f;
-  std::mutex jit_mutex_;
+  std::mutex jit_mutex_, cmp_mutex_;
   std::optional<double> cublas_gflops_, cublas_unfused_gflops_;
 };
 

@@ -6,6 +6,8 @@
 //
 //   tune     like `ptxforge-tune tune` (core/src/main.cpp:95-117) with a B200Runner:
 //            tune --dtype bf16 --M 8192 --N 8192 --K 8192 --gpus 1 --budget 30 --advisor rules --out t.json
+//            --fanout G measures up to G candidates per round, each on its own GPU(s) (tune_fanout.hpp);
+//            G = 1 (the default) is the reference's tune() unchanged
 //   measure  gate and time one config (like `ptxforge-tune bench`, core/src/main.cpp:224-238), one
 //            JSON line, exit 4 if the trial failed:
 //            measure --dtype bf16 --BM 128 --BN 256 --BK 32 --TM 4 --TN 16 --PAD 0 --M ... --gpus 2
@@ -19,6 +21,7 @@
 
 #include "ptxforge/search.hpp"
 #include "ptxforge_b200/b200_runner.hpp"
+#include "ptxforge_b200/tune_fanout.hpp"
 
 using namespace ptxforge;
 
@@ -68,6 +71,7 @@ B200Runner::Options runner_options(const Args &a) {
   o.workdir = a.get("workdir", "build/kernels");
   o.jit = a.get("jit", "1") != "0";
   o.cublas = a.get("cublas", "1") != "0";
+  o.fanout = a.geti("fanout", 1);
   return o;
 }
 
@@ -92,14 +96,15 @@ int cmd_tune(const Args &a) {
   o.budget = a.geti("budget", 30);
   o.seed = static_cast<uint64_t>(a.geti("seed", 0));
   o.log = [](const std::string &s) { std::puts(s.c_str()); };
-  json::Value tr = tune(prob, hw, runner, *advisor, o);
+  json::Value tr = tune_fanout(prob, hw, runner, *advisor, o, ro.fanout);
   const std::string out = a.get("out", "runs/trace_b200.json");
   const auto parent = std::filesystem::path(out).parent_path();
   if (!parent.empty()) std::filesystem::create_directories(parent);
   std::ofstream(out) << tr.dump(1);
   auto num = [&](const char *k) { return tr.at(k).is_null() ? std::string("n/a") : tr.at(k).dump(); };
-  std::printf("\nsource=%s dtype=%s gpus=%d space=%s configs trials=%zu\n", tr.at("source").as_string().c_str(),
-              pf_dtype_name(ro.dtype), ro.gpus, num("space_size").c_str(), tr.at("trials").size());
+  std::printf("\nsource=%s dtype=%s gpus=%d fanout=%d space=%s configs trials=%zu\n",
+              tr.at("source").as_string().c_str(), pf_dtype_name(ro.dtype), ro.gpus, ro.fanout,
+              num("space_size").c_str(), tr.at("trials").size());
   std::printf("baseline %s -> best %s GFLOP/s\ntrace -> %s\n", num("baseline_gflops").c_str(), num("best_gflops").c_str(),
               out.c_str());
   return 0;

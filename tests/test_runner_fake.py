@@ -138,6 +138,53 @@ def test_tune_trace_contract(tune_fake, tmp_path):
     assert ".entry" not in t["stages"][2]["text"]  # no compiler-written PTX embedded
 
 
+def tune_trace(tune_fake, tmp_path, name, *extra, **env):
+    out = tmp_path / name
+    r = run(tune_fake, ["tune", "--dtype", "bf16", *SMALL, "--budget", "12", "--advisor", "rules", "--out", str(out),
+                        *extra], **env)
+    assert r.returncode == 0, r.stderr
+    return json.loads(out.read_text())
+
+
+def test_tune_fanout_one_is_the_reference_tune(tune_fake, tmp_path):
+    # --fanout 1 (the default) calls ptxforge::tune itself: the trace carries no fan-out record
+    a = tune_trace(tune_fake, tmp_path, "a.json")
+    b = tune_trace(tune_fake, tmp_path, "b.json", "--fanout", "1")
+    assert "fanout" not in a
+    for t in (a, b):
+        del t["created"]
+    assert a == b
+
+
+@pytest.mark.parametrize("width,gpus", [(4, 1), (3, 2)])
+def test_tune_fanout_spreads_trials_over_gpus(tune_fake, tmp_path, width, gpus):
+    log = tmp_path / "calls.log"
+    seq = tune_trace(tune_fake, tmp_path, "seq.json", "--gpus", str(gpus))
+    fan = tune_trace(tune_fake, tmp_path, "fan.json", "--fanout", str(width), "--gpus", str(gpus), FAKE_PF_LOG=log)
+    # same schema-1 document, plus the fan-out record
+    assert set(fan) == set(seq) | {"fanout"}
+    assert fan["fanout"]["width"] == width and fan["fanout"]["rounds"] >= 12 // width
+    assert [set(t) for t in fan["trials"]] == [set(t) for t in seq["trials"]]
+    assert len(fan["trials"]) == 12
+    cfgs = [json.dumps(t["cfg"], sort_keys=True) for t in fan["trials"]]
+    assert len(set(cfgs)) == len(cfgs)
+    assert [t["i"] for t in fan["trials"]] == list(range(12))
+    # the seeding phase proposes tune()'s sequence: baseline, then the cost model's top picks (budget/4 = 3)
+    for s, f in zip(seq["trials"][:3], fan["trials"][:3]):
+        assert (s["cfg"], s["origin"]) == (f["cfg"], f["origin"])
+    assert fan["trials"][0]["origin"] == "baseline"
+    assert all(t["origin"] in ("baseline", "cost-model", "neighbor") or t["origin"].startswith("advisor:")
+               for t in fan["trials"])
+    # every trial slot's GPUs launched: slot s owns devices [s*gpus, (s+1)*gpus)
+    lines = log.read_text().split()
+    launched = {int(d) for what, d in zip(lines[::2], lines[1::2]) if what == "launch"}
+    assert launched == set(range(width * gpus))
+    # the cuBLAS comparator is measured once per problem and reported on every passing trial
+    assert fan["cublas_gflops"] is not None
+    assert all(t["cublas_gflops"] == fan["cublas_gflops"] for t in fan["trials"] if t["ok"])
+    assert sum(1 for what in lines[::2] if what == "cublas") == gpus
+
+
 def test_fp32_tile_outside_the_library_is_jit_compiled(tune_fake, tmp_path):
     # (64,32,8,4,4,0) is not precompiled: the runner nvcc's ptxforge_b200/csrc/simt_image.cu for it (as
     # CudaRunner compiles every config, cuda_runner.cpp:219-237) and loads it through pf_prepare_image.
