@@ -302,6 +302,45 @@ def run_ours(args, dist):
         hC.numpy().view(np.uint8).shape)) else 1.0) == 0.0
     ctx_e2e.close()
 
+    # optional all-gather of C's row shards (every rank ends with all of C), timed on its own and kept out
+    # of `value`: NCCL all_gather_into_tensor over NVLink
+    c_gather = None
+    if dist.world > 1:
+        from ptxforge_b200.sharded import RowGather
+        gat = RowGather(dist, w.M, w.N, out_bytes, tile[0])
+        gat(C)
+        torch.cuda.synchronize()
+
+        def checksum(block):
+            b = block.reshape(-1).view(torch.uint8).to(torch.int64)
+            return float((b * (torch.arange(b.numel(), device=b.device) % 65521 + 1)).sum().item())
+
+        row_bytes = w.N * out_bytes
+        full = gat.full()
+        mine = checksum(C.reshape(-1).view(torch.uint8)[:rows * row_bytes])
+        sums = torch.zeros(dist.world, dtype=torch.float64, device=C.device)
+        sums[dist.rank] = mine
+        dist.pg.all_reduce(sums)  # each rank's checksum of its own rows, everywhere
+        got = [checksum(full[s0:s0 + n]) for s0, n in gat.spans]
+        gather_ok = dist.max(0.0 if got == sums.tolist() else 1.0) == 0.0
+        n_g = 20
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        g0.record()
+        for _ in range(n_g):
+            gat(C)
+        g1.record()
+        g1.synchronize()
+        g_ms = dist.max(g0.elapsed_time(g1) / n_g)
+        c_bytes = w.M * w.N * out_bytes
+        c_gather = {"ms": round(g_ms, 4), "bytes_total": c_bytes, "bytes_received_per_rank": gat.bytes_per_rank(),
+                    "algbw_GBps": round(c_bytes / (g_ms * 1e-3) / 1e9, 1),
+                    "busbw_GBps": round(c_bytes * (dist.world - 1) / dist.world / (g_ms * 1e-3) / 1e9, 1),
+                    "op": "NCCL all_gather_into_tensor of each rank's C rows (ptxforge_b200.sharded.RowGather), "
+                          "after the kernel, outside the timed region of `value`",
+                    "matches_shards": gather_ok}
+        del gat, full
+
     attrs = ctx.attrs()
     comp = None
     if not args.no_comparators and dist.world == 1:
@@ -351,8 +390,10 @@ def run_ours(args, dist):
             "clocks": clk.summary(),
             "kernel": {"attrs": attrs},
         }
+        if c_gather:
+            res["c_allgather"] = c_gather
         if comp:
-            res["comparators"] = {k: {"ms": round(v, 4), "tflops": round(total_flops / (v * 1e-3) / 1e12, 2)}
+            res["comparators"] ={k: {"ms": round(v, 4), "tflops": round(total_flops / (v * 1e-3) / 1e12, 2)}
                                   for k, v in comp.items()}
         if dist.world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_sample(w, inp, args.cpu_seconds)

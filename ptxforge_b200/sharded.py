@@ -5,11 +5,13 @@ Instead of every rank copying all of B from host memory over its PCIe link, rank
 [r*Kp/world, (r+1)*Kp/world) of B (Kp = K rounded up to a multiple of world) and the slices are
 all-gathered over NVLink (NCCL, in place), so each input byte crosses PCIe once per step in total.
 Then the kernel runs on the local rows (no collective on the compute path) and the rank's rows of C go
-back to host memory.
+back to host memory.  RowGather is the optional, separately timed all-gather of C's row shards for
+consumers that need the whole result on every GPU.
 
     ranks = Ranks("nccl")
     run = ShardedHostGemm(ranks, "bf16", None, M, N, K)
     run(hA_rows, hB, hbias, hC_rows)                    # pinned host numpy/torch buffers
+    whole_c = RowGather(ranks, M, N, 2, 256)(c_rows_on_device).full()
 """
 from __future__ import annotations
 
@@ -87,3 +89,63 @@ class ShardedHostGemm:
 
     def close(self):
         self.ctx.close()
+
+
+class RowGather:
+    """Optional all-gather of C's row shards, so that every rank holds the whole M x N result.
+
+    The compute path has no collective; a consumer that needs all of C on one GPU calls this after the
+    kernel, as a separate, separately timed step.  Every rank contributes the `rows` x N block it owns
+    (`shard_span(M, world, rank, align)`).  When all shards have the same height the gathered buffer
+    already is C, row-major; otherwise each rank's block sits in a slot of the tallest shard's height and
+    `full()` packs the blocks together.  NCCL (`all_gather_into_tensor`, over NVLink on one box) for GPU
+    tensors; the list form of all_gather for gloo ranks on the CPU.
+    """
+
+    def __init__(self, ranks: Ranks, M: int, N: int, out_bytes: int, align: int, device=None):
+        import torch
+
+        self.torch = torch
+        self.ranks = ranks
+        self.N, self.o = N, out_bytes
+        self.spans = [shard_span(M, ranks.world, r, align) for r in range(ranks.world)]
+        self.slot_rows = max(1, max(n for _, n in self.spans))
+        self.equal = all(n == self.slot_rows for _, n in self.spans)
+        self.slot_bytes = self.slot_rows * N * out_bytes
+        dev = device if device is not None else torch.device("cuda", ranks.local_rank)
+        self.buf = torch.empty(ranks.world * self.slot_bytes, dtype=torch.uint8, device=dev)
+        self.send = None if self.equal else torch.zeros(self.slot_bytes, dtype=torch.uint8, device=dev)
+
+    def bytes_per_rank(self) -> int:
+        """Bytes of C each rank receives from the others in one gather."""
+        me = self.ranks.rank
+        return sum(n for r, (_, n) in enumerate(self.spans) if r != me) * self.N * self.o
+
+    def __call__(self, c_rows):
+        """Gather: `c_rows` is this rank's rows x N block of C (any dtype, contiguous, on the device)."""
+        torch = self.torch
+        mine = c_rows.reshape(-1).view(torch.uint8)
+        rows = self.spans[self.ranks.rank][1]
+        if mine.numel() < rows * self.N * self.o:
+            raise ValueError("c_rows holds fewer bytes than this rank's shard of C")
+        src = mine[:self.slot_bytes] if self.equal else self.send
+        if not self.equal:
+            src[:rows * self.N * self.o].copy_(mine[:rows * self.N * self.o])
+        pg = self.ranks.pg
+        if pg is None or self.ranks.world == 1:
+            self.buf.copy_(src)
+        elif self.ranks.backend == "nccl":
+            pg.all_gather_into_tensor(self.buf, src)
+        else:
+            pg.all_gather(list(self.buf.split(self.slot_bytes)), src)
+        return self
+
+    def full(self):
+        """The gathered C as M x N * out_bytes uint8 rows (a view when all shards have the same height)."""
+        torch = self.torch
+        row = self.N * self.o
+        if self.equal:
+            return self.buf.view(-1, row)
+        parts = [self.buf[r * self.slot_bytes:r * self.slot_bytes + n * row].view(-1, row)
+                 for r, (_, n) in enumerate(self.spans) if n]
+        return torch.cat(parts)
