@@ -206,3 +206,75 @@ def test_fp32_tile_that_does_not_compile_is_a_failed_trial(tune_fake, tmp_path):
     r = run(tune_fake, args)
     j = json.loads(r.stdout.strip().splitlines()[-1])
     assert r.returncode == 4 and not j["ok"] and j["error"].startswith("nvcc failed")
+
+
+FAKE_NCU = """#!/bin/bash
+# stands in for ncu: checks the flags the capture must carry, runs the profiled command, writes a CSV
+args=("$@"); log=""; cmd=()
+for ((i=0; i<${#args[@]}; i++)); do
+  case "${args[$i]}" in
+    --log-file) log="${args[$((i+1))]}"; i=$((i+1));;
+    --metrics|-k|-c|--clock-control) i=$((i+1));;
+    --csv) ;;
+    *) cmd=("${args[@]:$i}"); break;;
+  esac
+done
+echo "$*" > "$log.args"
+"${cmd[@]}" > /dev/null || exit 9
+cat > "$log" <<CSV
+==PROF== Connected to process 1
+"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream","Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"
+"0","1","tune","h","void pf::gemm_bias_gelu_tc<x>(p)","1","7","(192, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_read.sum","byte","1,048,576"
+"0","1","tune","h","void pf::gemm_bias_gelu_tc<x>(p)","1","7","(192, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_write.sum","byte","131072"
+"0","1","tune","h","void pf::gemm_bias_gelu_tc<x>(p)","1","7","(192, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed","%","61.5"
+"1","1","tune","h","void pf::gemm_bias_gelu_tc<x>(p)","1","7","(192, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_read.sum","byte","7"
+CSV
+"""
+
+
+def test_ncu_counters_attached_to_the_trace(tune_fake, tmp_path):
+    """ptxforge_b200.counters: plain run first, ncu with clocks left alone on one launch, counters in the trace."""
+    from ptxforge_b200 import counters
+
+    exe, _ = tune_fake
+    trace_path = tmp_path / "t.json"
+    r = run(tune_fake, ["tune", "--dtype", "bf16", *SMALL, "--budget", "4", "--out", str(trace_path)])
+    assert r.returncode == 0, r.stderr
+    ncu = tmp_path / "ncu"
+    ncu.write_text(FAKE_NCU)
+    ncu.chmod(0o755)
+    out = tmp_path / "t_counters.json"
+    rc = counters.main(["--trace", str(trace_path), "--out", str(out), "--exe", exe, "--ncu", str(ncu),
+                        "--root", ROOT])
+    assert rc == 0
+    t = json.loads(out.read_text())
+    c = t["counters"]
+    assert c["metrics"]["dram__bytes_read.sum"] == 1048576  # first launch only, thousands separators read
+    assert c["metrics"]["sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed"] == 61.5
+    assert c["derived"]["dram_bytes"] == 1048576 + 131072
+    algo = (256 * 128 + 128 * 256) * 2 + 256 * 4 + 256 * 256 * 2
+    assert c["derived"]["algorithmic_bytes"] == algo
+    assert c["derived"]["measured_ai"] == round(2.0 * 256 * 256 * 128 / (1048576 + 131072), 2)
+    assert t["trials"][t["best_index"]]["counters"] == c["metrics"]
+    assert c["cfg"] == t["trials"][t["best_index"]]["cfg"]
+    args = (tmp_path / "t_counters.ncu.csv.args").read_text()
+    assert "--clock-control none" in args and "-c 1" in args and "-k regex:gemm_bias_gelu" in args
+    assert "measure" in args and "--cublas 0" in args
+
+
+def test_ncu_counters_refuse_when_the_plain_run_fails(tune_fake, tmp_path):
+    from ptxforge_b200 import counters
+
+    exe, _ = tune_fake
+    trace_path = tmp_path / "t.json"
+    r = run(tune_fake, ["tune", "--dtype", "bf16", *SMALL, "--budget", "3", "--out", str(trace_path)])
+    assert r.returncode == 0, r.stderr
+    ncu = tmp_path / "ncu"
+    ncu.write_text("#!/bin/bash\ntouch " + str(tmp_path / "ncu_ran") + "\n")
+    ncu.chmod(0o755)
+    os.environ["FAKE_PF_FAIL_LAUNCH"] = "1"
+    try:
+        rc = counters.main(["--trace", str(trace_path), "--exe", exe, "--ncu", str(ncu)])
+    finally:
+        del os.environ["FAKE_PF_FAIL_LAUNCH"]
+    assert rc == 2 and not (tmp_path / "ncu_ran").exists()
