@@ -38,6 +38,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "TFLOP/s fused GEMM+bias+GELU bf16 8192³, % B200 dense peak, at 1/2/4/8 GPUs"
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+PEAK_NOTE = {"bf16": "bf16_tflops", "e4m3": "bf16_tflops x 2, the fp8 rate",
+             "f32_3xtf32": "bf16_tflops / 2 (the tf32 rate) / 3 (tf32 products per fp32 product)",
+             "f32": "SIMT FFMA nominal, 148 SMs x 128 lanes x 2 x 1.965 GHz"}
 
 
 def parse_args():
@@ -158,8 +161,9 @@ def Dist(n_gpus: int):
 # our arm
 # ------------------------------------------------------------------------------------------------
 def device_operands(torch, w, inp, r0, rows):
-    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "e4m3": torch.float8_e4m3fn}[w.dtype]
-    out_dt = torch.float32 if w.dtype == "f32" else torch.bfloat16
+    dt = {"f32": torch.float32, "f32_3xtf32": torch.float32, "bf16": torch.bfloat16,
+          "e4m3": torch.float8_e4m3fn}[w.dtype]
+    out_dt = torch.float32 if w.dtype in ("f32", "f32_3xtf32") else torch.bfloat16
 
     def dev(x):
         t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
@@ -272,7 +276,7 @@ def run_ours(args, dist):
                         pin_memory=True)
         t.numpy().view(arr.dtype)[...] = arr
         pin[name] = t
-    out_bytes = 4 if w.dtype == "f32" else 2
+    out_bytes = 4 if w.dtype in ("f32", "f32_3xtf32") else 2
     hC = torch.empty((rows, w.N), dtype=torch.float32 if out_bytes == 4 else torch.int16, pin_memory=True)
     if dist.world == 1:
         # one GPU: pf_run_host (C ABI), row chunks whose copies and kernels overlap
@@ -355,10 +359,12 @@ def run_ours(args, dist):
         value = total_flops / (ms * 1e-3) / 1e12
         per_gpu_flops = 2.0 * rows * w.N * w.K
         achieved = per_gpu_flops / (ms_local * 1e-3) / 1e12
-        peak_key = {"bf16": "bf16_tflops", "e4m3": "bf16_tflops", "f32": None}[w.dtype]
+        peak_key = {"bf16": "bf16_tflops", "e4m3": "bf16_tflops", "f32_3xtf32": "bf16_tflops", "f32": None}[w.dtype]
         peak = pk.get(peak_key) if peak_key else None
         if w.dtype == "e4m3" and peak:
             peak = 2.0 * peak  # fp8 dense rate is twice bf16 on the same tensor cores
+        if w.dtype == "f32_3xtf32" and peak:
+            peak = peak / 2.0 / 3.0  # tf32 runs at half the bf16 rate; three tf32 products per fp32 product
         if w.dtype == "f32":
             peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SIMT FFMA peak at max SM clock
         traffic = None
@@ -378,7 +384,7 @@ def run_ours(args, dist):
             "pct_of_peak": round(100.0 * value / (peak * dist.world), 2) if peak else None,
             "roofline": {"bound": "tensor" if w.dtype != "f32" else "fp32-simt", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if peak else None,
-                         "peak_source": f"{pk_kind} ({peak_key or 'SIMT nominal'}; burst, kernel timed alone)",
+                         "peak_source": f"{pk_kind} ({PEAK_NOTE[w.dtype]}; burst, kernel timed alone)",
                          "traffic": traffic,
                          "algorithmic_bytes": w.algorithmic_bytes()},
             "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",

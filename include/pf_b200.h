@@ -48,7 +48,9 @@ enum {
 /* ---- data types --------------------------------------------------------------------------- */
 typedef enum {
   PF_F32 = 0,          /* fp32 A/B/C, fp32 FFMA (SIMT) accumulate, tanhf epilogue               */
-  PF_F32_3XTF32 = 1,   /* reserved: fp32 via three tf32 tensor-core products (not built yet)    */
+  PF_F32_3XTF32 = 1,   /* fp32 A/B/C; each operand split into tf32 hi + lo, three tf32
+                        * tensor-core products per step (lo*hi + hi*lo + hi*hi), fp32 accumulate
+                        * in TMEM, tanhf epilogue: fp32-path tolerance at tensor-core speed      */
   PF_BF16 = 2,         /* bf16 A/B, fp32 accumulate in TMEM, bf16 C                             */
   PF_E4M3 = 3          /* fp8 e4m3 A/B with per-tensor fp32 scales, fp32 accumulate, bf16 C     */
 } pf_dtype;
@@ -60,7 +62,9 @@ typedef enum {
  *                 swizzle row); TM = requested pipeline depth in stages (clamped to the deepest
  *                 compiled variant that fits shared memory); TN = tile-raster group height in M
  *                 blocks (consecutive tiles walk TN row blocks before moving along N); PAD = extra
- *                 128-byte k-atoms per stage (0: one atom = 64 bf16 / 128 e4m3 k, 1: two atoms). */
+ *                 128-byte k-atoms per stage (0: one atom = 64 bf16 / 128 e4m3 k, 1: two atoms).
+ *   3xTF32 path : BM = BN = 256 (a CTA pair), BK = 32 (one 128-byte row of fp32 k), TM = stages
+ *                 (2 or 3, clamped), TN = raster group, PAD = 0. */
 typedef struct {
   int BM, BN, BK, TM, TN, PAD;
 } pf_tile;
@@ -110,7 +114,7 @@ int pf_prepare_image(pf_ctx *ctx, const void *image, size_t image_bytes, const c
                      int grid_y, int block, int M, int N, int K);
 
 /* Bind caller-owned device operands (row-major).  A/B are float, bf16 or e4m3 bytes according to
- * the prepared dtype; C is float for PF_F32 and bf16 otherwise.  scale_a/scale_b are the
+ * the prepared dtype; C is float for PF_F32 and PF_F32_3XTF32 and bf16 otherwise.  scale_a/scale_b are the
  * per-tensor dequantisation scales (used by PF_E4M3, must be 1 otherwise).  Replaces the
  * parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} of cuda_runner.cpp:182. */
 int pf_bind(pf_ctx *ctx, const void *A, const void *B, const float *bias, void *C, float scale_a,
@@ -140,7 +144,7 @@ int pf_attrs(pf_ctx *ctx, pf_attr *out);
 
 /* Synchronise the device and read (then clear) the context's device status word: 0 = clean,
  * nonzero = a bounded device-side wait ran out (bit 0: TMA-producer wait, bit 1: MMA wait,
- * bit 2: epilogue wait, bit 3: teardown wait). */
+ * bit 2: epilogue wait, bit 3: teardown wait, bit 4: 3xTF32 split wait). */
 int pf_device_status(pf_ctx *ctx, unsigned *err_word);
 
 /* Stream-K tail of the CTA-pair (BM=256) kernel: -1 auto (default: used with at least 3 waves of tiles

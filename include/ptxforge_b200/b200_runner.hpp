@@ -42,9 +42,13 @@
 namespace ptxforge {
 
 // hw.hpp has no B200 row (core/include/ptxforge/hw.hpp:36-49).  peak_gflops is the dense rate of the
-// dtype the runner measures; smem_per_block is the sm_100 opt-in limit (232,448 B).
+// dtype the runner measures (3xTF32: the tf32 rate over its three products per fp32 product);
+// smem_per_block is the sm_100 opt-in limit (232,448 B).
 inline GPU b200_gpu(pf_dtype dtype = PF_BF16) {
-  const double peak = dtype == PF_E4M3 ? 4.5e6 : dtype == PF_BF16 ? 2.25e6 : 74.4e3;
+  const double peak = dtype == PF_E4M3          ? 4.5e6
+                      : dtype == PF_BF16        ? 2.25e6
+                      : dtype == PF_F32_3XTF32  ? 1.125e6 / 3
+                                                : 74.4e3;
   return GPU{"b200", "NVIDIA B200", "sm_100a", 148, peak, 8000, 65536, 2048, 32, 233472, 232448, 0.75};
 }
 
@@ -116,6 +120,9 @@ class B200Runner : public Runner {
     if (opt_.dtype == PF_BF16 || opt_.dtype == PF_E4M3) {
       t.BK = 32;
       t.PAD = c.PAD >= 1 ? 1 : 0;
+    } else if (opt_.dtype == PF_F32_3XTF32) {
+      t.BK = 32;
+      t.PAD = 0;
     }
     return t;
   }
@@ -283,7 +290,9 @@ class B200Runner : public Runner {
     // Source only.  Compiler-written PTX/SASS of this build is never embedded in a trace.
     const std::string dir = opt_.root + "/ptxforge_b200/csrc/";
     const bool tensor = opt_.dtype == PF_BF16 || opt_.dtype == PF_E4M3;
-    const std::string file = !tensor ? "gemm_simt.cuh" : (c.BM == 256 ? "gemm_tc2.cuh" : "gemm_tc.cuh");
+    const std::string file = opt_.dtype == PF_F32_3XTF32 ? "gemm_tf32x3.cuh"
+                             : !tensor                   ? "gemm_simt.cuh"
+                             : (c.BM == 256 ? "gemm_tc2.cuh" : "gemm_tc.cuh");
     std::string src;
     try {
       src = read_file(dir + file);

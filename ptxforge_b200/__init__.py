@@ -55,9 +55,11 @@ class Attr(ctypes.Structure):
 
 # Best-measured defaults per dtype.  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
 # stage (PAD=1) and as many stages as fit (TM=8 -> 3), raster group 8 M-blocks (TN=8) -- the lowest energy
-# per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4.
+# per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4; 3xTF32: CTA pair,
+# 3 stages, raster group 8.
 DEFAULT_TILES = {
     "f32": (128, 128, 8, 8, 8, 4),
+    "f32_3xtf32": (256, 256, 32, 3, 8, 0),
     "bf16": (256, 256, 32, 8, 8, 1),
     "e4m3": (256, 256, 32, 8, 8, 1),
 }
@@ -290,8 +292,9 @@ def gemm_bias_gelu(A, B, bias, C=None, *, dtype: str | None = None, tile=None, s
                    scale_b: float = 1.0, stream=None):
     """C = gelu_tanh(scale_a*scale_b * A @ B + bias) for CUDA torch tensors (row-major, contiguous).
 
-    dtype: "f32" (A, B, C float32), "bf16" (A, B bfloat16, C bfloat16) or "e4m3" (A, B float8_e4m3fn or
-    uint8 codes, C bfloat16).  bias is float32 [N].  Returns C.
+    dtype: "f32" (A, B, C float32; SIMT FFMA), "f32_3xtf32" (the same operands on the tensor cores, three
+    TF32 products per step), "bf16" (A, B bfloat16, C bfloat16) or "e4m3" (A, B float8_e4m3fn or uint8
+    codes, C bfloat16).  bias is float32 [N].  Returns C.
     """
     import torch
 
@@ -306,7 +309,7 @@ def gemm_bias_gelu(A, B, bias, C=None, *, dtype: str | None = None, tile=None, s
             raise ValueError("operands must be contiguous CUDA tensors")
     if bias.dtype != torch.float32:
         raise ValueError("bias must be float32")
-    out_dtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    out_dtype = torch.float32 if OUT_BYTES[dtype] == 4 else torch.bfloat16
     if C is None:
         C = torch.empty((M, N), dtype=out_dtype, device=A.device)
     ctx = context(A.device.index or 0)

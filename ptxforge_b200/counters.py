@@ -39,8 +39,9 @@ METRICS = [
     "smsp__sass_thread_inst_executed_op_ffma_pred_on.sum",
 ]
 
-ELEM_BYTES = {"f32": 4, "bf16": 2, "e4m3": 1}
-OUT_BYTES = {"f32": 4, "bf16": 2, "e4m3": 2}
+ELEM_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 1}
+OUT_BYTES = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 2}
+DTYPE_OF_PEAK = {4.5e6: "e4m3", 2.25e6: "bf16", 375000.0: "f32_3xtf32"}  # b200_gpu()'s peak_gflops
 
 
 def best_trial(trace: dict) -> dict:
@@ -137,7 +138,7 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     with open(a.trace) as f:
         trace = json.load(f)
-    dtype = a.dtype or {4.5e6: "e4m3", 2.25e6: "bf16"}.get(trace["gpu"].get("peak_gflops"), "f32")
+    dtype = a.dtype or DTYPE_OF_PEAK.get(trace["gpu"].get("peak_gflops"), "f32")
     out = a.out or a.trace
     csv_path = a.csv or os.path.splitext(out)[0] + ".ncu.csv"
     cmd = measure_command(a.exe, trace, dtype, root=a.root)

@@ -160,7 +160,7 @@ extern "C" int pf_time_cublas(pf_ctx *c, int warmup, int iters, int reps, double
   if (!lt.ok) return set_err(c, PF_ECUDA, "cuBLAS comparator unavailable: %s", lt.err.c_str());
   DeviceGuard g(c->device);
   const int M = c->M, N = c->N, K = c->K;
-  const bool f8 = c->dtype == PF_E4M3, f32 = c->dtype == PF_F32;
+  const bool f8 = c->dtype == PF_E4M3, f32 = c->dtype == PF_F32 || c->dtype == PF_F32_3XTF32;
   const size_t ob = pf_out_bytes(c->dtype);
   int rc;
   if (!c->lt_handle) {

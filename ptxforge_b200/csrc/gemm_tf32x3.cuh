@@ -1,0 +1,342 @@
+// gemm_tf32x3.cuh -- the fp32 fused GEMM + bias + GELU on the tensor cores: 3xTF32 on CTA pairs.
+//
+// The reference kernel is fp32 FFMA (kernels/gemm_bias_gelu.cu:42-98).  This kernel keeps fp32 inputs
+// and an fp32 result but does the contraction on the TF32 tensor cores with the split-precision
+// ("3xTF32") method (Ootomo & Yokota, "Recovering single precision accuracy from Tensor Cores while
+// surpassing the FP32 theoretical peak performance", IJHPCA 2022; CUTLASS's tfloat32x3 GEMMs):
+// every element is split in shared memory into
+//     hi = x with its 13 low mantissa bits cleared   (exactly a TF32 value)
+//     lo = x - hi                                     (exact in fp32, |lo| < 2^-10 |x|)
+// and a*b is accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b (tcgen05.mma kind::tf32, fp32 in TMEM).
+// The dropped lo_a*lo_b term is below 2^-20 |a*b| and the TF32 reading of lo loses at most 2^-21 |x|,
+// so each product is good to ~2^-19 relative -- inside the fp32 path's 1e-5 tolerance, with the
+// epilogue's GELU in the reference's own form (tanhf), not the MUFU approximation of the bf16 path.
+//
+// CTA pairs (cluster of 2, tcgen05 .cta_group::2, M = 256, N = 256), persistent, 320 threads per CTA:
+//   warp 0      TMA producer (both CTAs): its own A rows [m0 + 128*rank, +128) and B columns
+//               [n0 + 128*rank, +128) of one 32-k block (128-byte swizzled rows) into its own stage,
+//               counted on its own `full` barrier (no multicast);
+//   warps 6-9   split (both CTAs): wait for `full`, rewrite the stage in place as hi and write lo to the
+//               stage's second half (same swizzled layout, element by element), fence the writes to the
+//               async proxy and arrive on the leader's `ready` barrier (4 warps x 2 CTAs);
+//   warp 1      leader lane: waits `ready`, issues the three MMAs per 8-k step, commits the stage free
+//               (multicast to both CTAs) and the finished accumulator to both epilogues;
+//   warps 2-5   epilogue (both CTAs): tcgen05.ld 32 columns at a time, + bias[c], GELU, fp32 through a
+//               128-byte-swizzled 32 x 32 box and a TMA store; the accumulator (double-buffered, 2 x 256
+//               TMEM columns) goes back to the MMA lane right after its last load.
+// Shared memory per CTA and stage: 32 KB of hi (A 16 KB + B 16 KB) and 32 KB of lo; 3 stages.
+#pragma once
+
+#include "gemm_tc2.cuh"
+
+namespace pf {
+
+template <int kStages>
+struct Tf32x3Config {
+  static constexpr int BM = 256;                             // pair tile rows
+  static constexpr int BM_CTA = 128;
+  static constexpr int BN = 256;                             // pair tile columns (UMMA N)
+  static constexpr int BN_CTA = 128;                         // B columns loaded by each CTA
+  static constexpr int STAGES = kStages;
+  static constexpr int ELEM = 4;
+  static constexpr int ATOM_K = 32;                          // fp32 elements in one 128-byte row
+  static constexpr int BK = ATOM_K;                          // k per stage
+  static constexpr int UMMA_K = 8;                           // k per kind::tf32 MMA (32 bytes)
+  static constexpr int A_BYTES = BM_CTA * 128;               // 128 rows x 128 B
+  static constexpr int B_CHUNK_N = 32;                       // N elements per 128-byte row of B
+  static constexpr int B_CHUNKS = BN_CTA / B_CHUNK_N;
+  static constexpr int B_CHUNK_BYTES = BK * 128;
+  static constexpr int B_BYTES = B_CHUNKS * B_CHUNK_BYTES;
+  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;        // what TMA brings in (then hi, in place)
+  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;          // hi + lo
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int SPLIT_WARPS = 4;
+  static constexpr int EPI_COLS = 32;                        // fp32 columns per TMA store box (128 B)
+  static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 4;    // 32 rows x 128 B
+  static constexpr int EPI_BUFS = 2;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
+  static constexpr int NUM_BARS = 3 * STAGES + 4 + 1;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS + SPLIT_WARPS);
+  static constexpr uint32_t IDESC = instr_desc(2u, 2u, /*A K-major*/ 0u, /*B MN-major*/ 1u, 256, 256);
+  static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
+};
+
+enum : unsigned { kErrSplitWait = 16u };
+
+// 0.5*x*(1 + tanh(k0*(x + k1*x^3))) as the reference writes it (kernels/gemm_bias_gelu.cu:37-40).
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+template <class Cfg>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
+    gemm_bias_gelu_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  // stage s: [hi A | hi B | lo A | lo B], each half RAW_BYTES, all 1024-byte aligned
+  auto stage_hi = [&](int s) { return smem + s * Cfg::STAGE_BYTES; };
+  auto stage_lo = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_BYTES; };
+  uint8_t *sEpi = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + Cfg::EPI_BYTES);
+  uint64_t *full = bars;                        // [STAGES] own: this CTA's TMA bytes landed
+  uint64_t *ready = bars + Cfg::STAGES;         // [STAGES] leader: both CTAs' stages split
+  uint64_t *empty = bars + 2 * Cfg::STAGES;     // [STAGES] both: MMAs reading the stage finished
+  uint64_t *tfull = bars + 3 * Cfg::STAGES;     // [2] both: accumulator ready
+  uint64_t *tempty = tfull + 2;                 // [2] leader: both CTAs drained the accumulator
+  uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();      // 0 = leader, 1 = follower
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 2 * Cfg::SPLIT_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * Cfg::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+    tc_fence_before();
+  }
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  auto fail = [&](unsigned bit) {
+    atomicOr(p.status, bit);
+    *abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
+        const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
+            fail(kErrProducerWait);
+            ok = false;
+            break;
+          }
+          uint8_t *dst = stage_hi(stage);
+          mbar_arrive_expect_tx(&full[stage], Cfg::RAW_BYTES);
+          tma_load_2d(dst, &tmA, &full[stage], kb * Cfg::BK, m0);
+#pragma unroll
+          for (int j = 0; j < Cfg::B_CHUNKS; ++j)
+            tma_load_2d(dst + Cfg::A_BYTES + j * Cfg::B_CHUNK_BYTES, &tmB, &full[stage], n0 + j * Cfg::B_CHUNK_N,
+                        kb * Cfg::BK);
+          ++issued;
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Loads already issued land before the block may exit (bounded).
+        for (int s = 0; s < Cfg::STAGES && s < issued; ++s) {
+          const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+          volatile int no_abort = 0;
+          if (!mbar_wait(&full[s], ph, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+        }
+      }
+    }
+  } else if (warp >= 2 + Cfg::EPI_WARPS) {
+    // ---------------------------------------------------------------- split hi / lo (warps 6..9)
+    const int tid = threadIdx.x - 32 * (2 + Cfg::EPI_WARPS);
+    const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready[0]), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const bool waited = mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag);
+        if (!__all_sync(0xffffffffu, waited)) {
+          if (lane == 0) fail(kErrSplitWait);
+          ok = false;
+          break;
+        }
+        const uint32_t hi = smem_u32(stage_hi(stage));
+        const uint32_t lo = smem_u32(stage_lo(stage));
+#pragma unroll 4
+        for (int i = tid; i < Cfg::RAW_BYTES / 16; i += 32 * Cfg::SPLIT_WARPS) {
+          uint32_t x0, x1, x2, x3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3)
+                       : "r"(hi + i * 16));
+          const uint32_t h0 = x0 & 0xFFFFE000u, h1 = x1 & 0xFFFFE000u, h2 = x2 & 0xFFFFE000u, h3 = x3 & 0xFFFFE000u;
+          st_shared_v4(hi + i * 16, h0, h1, h2, h3);
+          st_shared_v4(lo + i * 16, __float_as_uint(__uint_as_float(x0) - __uint_as_float(h0)),
+                       __float_as_uint(__uint_as_float(x1) - __uint_as_float(h1)),
+                       __float_as_uint(__uint_as_float(x2) - __uint_as_float(h2)),
+                       __float_as_uint(__uint_as_float(x3) - __uint_as_float(h3)));
+        }
+        // The tensor cores read shared memory through the async proxy.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(ready_leader0 + stage * 8);
+        if (++stage == Cfg::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+          fail(kErrMmaWait);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&ready[stage], phase, p.timeout_ns, abort_flag)) {
+            fail(kErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(stage_hi(stage)), a_lo = smem_u32(stage_lo(stage));
+          const uint32_t b_hi = a_hi + Cfg::A_BYTES, b_lo = a_lo + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+            // A: K-major, k advances 32 bytes inside the swizzle row.  B: N-major, k advances 8 rows
+            // of 128 B; LBO = the next 32-column chunk.
+            const uint64_t ah = smem_desc(a_hi + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t al = smem_desc(a_lo + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bh = smem_desc(b_hi + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+            const uint64_t bl = smem_desc(b_lo + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+            // small terms first
+            tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
+            tc_mma_tf32_pair(d_tmem, ah, bh, Cfg::IDESC, 1u);
+          }
+          tc_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      tc_commit_pair(drain);
+      volatile int no_abort = 0;
+      if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    const int ew = warp - 2;
+    uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, waited)) {
+        if (lane == 0) fail(kErrEpilogueWait);
+        break;
+      }
+      tc_fence_after();
+      const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
+      const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[acc]), 0);
+#pragma unroll 1
+      for (int c = 0; c < Cfg::BN / Cfg::EPI_COLS; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS, v);
+        tmem_ld_wait();
+        if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
+          // Last TMEM read of this accumulator: hand it back to the MMA issuer.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader);
+        }
+        const int n0 = nb * Cfg::BN + c * Cfg::EPI_COLS;
+        const uint32_t sbuf = smem_u32(ebuf + buf * Cfg::EPI_BUF_BYTES) + lane * 128;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
+          const float y0 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 0]) + b4.x);
+          const float y1 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 1]) + b4.y);
+          const float y2 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 2]) + b4.z);
+          const float y3 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 3]) + b4.w);
+          // row `lane` of the 32 x 32 fp32 box: 16-byte chunk j4 goes to chunk j4 ^ (row % 8)
+          st_shared_v4(sbuf + static_cast<uint32_t>((j4 ^ (lane & 7)) * 16), __float_as_uint(y0), __float_as_uint(y1),
+                       __float_as_uint(y2), __float_as_uint(y3));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, ebuf + buf * Cfg::EPI_BUF_BYTES, n0, m0);
+          tma_store_commit();
+          tma_store_wait_read<1>();
+        }
+        __syncwarp();
+        buf ^= 1;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace pf

@@ -22,6 +22,7 @@
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tf32x3.cuh"
 
 #ifndef PF_VERSION_STR
 #define PF_VERSION_STR "0.1.0"
@@ -50,6 +51,7 @@ struct Variant {
   int a_box_k = 0;              // k elements per TMA box of A (one 128-byte swizzle row)
   int katoms = 1;               // 128-byte k-atoms per pipeline stage
   int cta_per_tile = 1;         // 2 = CTA-pair (cluster) kernel
+  bool stream_k = false;        // the kernel can run a stream-K tail
   int b_chunk_n = 0;
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                     const TcParams &) = nullptr;
@@ -116,7 +118,37 @@ Variant make_tc2_variant() {
   v.a_box_k = Cfg::ATOM_K;
   v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 2;
+  v.stream_k = true;
   v.launch_tc = &launch_tc2_impl<DT, ST, KA>;
+  return v;
+}
+
+template <int ST>
+void launch_tf32x3_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                        const TcParams &p) {
+  using Cfg = pf::Tf32x3Config<ST>;
+  pf::gemm_bias_gelu_tf32x3<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+}
+
+template <int ST>
+Variant make_tf32x3_variant() {
+  using Cfg = pf::Tf32x3Config<ST>;
+  Variant v;
+  v.path = Path::kTensor;
+  v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tf32x3<Cfg>);
+  v.threads = Cfg::THREADS;
+  v.smem = Cfg::SMEM_BYTES;
+  v.bm = Cfg::BM;
+  v.bn = Cfg::BN;
+  v.bk_elems = Cfg::BK;
+  v.stages = Cfg::STAGES;
+  v.elem = Cfg::ELEM;
+  v.b_chunk_n = Cfg::B_CHUNK_N;
+  v.a_box_rows = Cfg::BM_CTA;
+  v.a_box_k = Cfg::ATOM_K;
+  v.katoms = 1;
+  v.cta_per_tile = 2;
+  v.launch_tc = &launch_tf32x3_impl<ST>;
   return v;
 }
 
@@ -187,6 +219,7 @@ bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant
       {PF_E4M3, 128, 128, 6, 1, &make_tc_variant<1, 128, 6>},     {PF_E4M3, 256, 256, 2, 1, &make_tc2_variant<1, 2>},
       {PF_E4M3, 256, 256, 4, 1, &make_tc2_variant<1, 4>},         {PF_E4M3, 256, 256, 6, 1, &make_tc2_variant<1, 6>},
       {PF_E4M3, 256, 256, 3, 2, &make_tc2_variant<1, 3, 2>},
+      {PF_F32_3XTF32, 256, 256, 2, 1, &make_tf32x3_variant<2>}, {PF_F32_3XTF32, 256, 256, 3, 1, &make_tf32x3_variant<3>},
   };
   const Entry *best = nullptr;
   for (const Entry &e : table)
@@ -349,10 +382,25 @@ int encode_2d(pf_ctx *c, CUtensorMap *map, CUtensorMapDataType dt, const void *b
   return PF_OK;
 }
 
+// Element types of the tensor path's TMA maps: A and B in the dtype's encoding; C is bf16 except on the
+// 3xTF32 path (fp32).  A C box is one 128-byte row of columns by 32 rows (one epilogue warp).
+CUtensorMapDataType in_map_type(pf_dtype dt) {
+  return dt == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                       : dt == PF_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+CUtensorMapDataType out_map_type(pf_dtype dt) {
+  return dt == PF_F32_3XTF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+int encode_c_map(pf_ctx *c, CUtensorMap *map, void *C, int rows) {
+  const uint64_t o = pf_out_bytes(c->dtype);
+  return encode_2d(c, map, out_map_type(c->dtype), C, c->N, rows, c->N * o, static_cast<uint32_t>(128 / o), 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 int encode_maps(pf_ctx *c) {
   const Variant &v = c->var;
-  const CUtensorMapDataType in_t =
-      (c->dtype == PF_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType in_t = in_map_type(c->dtype);
   const uint64_t e = static_cast<uint64_t>(v.elem);
   int rc;
   // A: [M x K], K contiguous; box = BK elements (128 B) x BM rows.
@@ -361,10 +409,8 @@ int encode_maps(pf_ctx *c) {
   // B: [K x N], N contiguous; box = 128 B of N x BK rows.
   rc = encode_2d(c, &c->tmB, in_t, c->B, c->N, c->K, c->N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  // C: [M x N] bf16; box = 64 columns (128 B) x 32 rows (one epilogue warp).
-  rc = encode_2d(c, &c->tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c->C, c->N, c->M, c->N * 2ull, 64, 32,
-                 CU_TENSOR_MAP_SWIZZLE_128B);
-  return rc;
+  // C: [M x N]; box = 128 B of columns x 32 rows.
+  return encode_c_map(c, &c->tmC, c->C, c->M);
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -376,7 +422,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // us).  Below 2 waves the per-pair fixed costs (pipeline fill, the head's wait and partial reads, the
 // last epilogue) outweigh the rebalancing (1024-row shards: 105 -> 111 us), so auto stays data-parallel.
 int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
-  if (c->var.cta_per_tile != 2 || c->stream_k == 0) return 0;
+  if (!c->var.stream_k || c->stream_k == 0) return 0;
   const int W = c->max_units;
   const int R = tiles % W;
   if (R == 0 || static_cast<long long>(R) * k_blocks < W) return 0;
@@ -649,6 +695,18 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     if ((static_cast<long long>(N) * e) % 16 != 0 || (N * 2) % 16 != 0)
       return set_err(c, PF_ESHAPE, "tensor path: rows of B and C must be multiples of 16 bytes (N=%d)", N);
     c->group_m = t->TN;
+  } else if (dt == PF_F32_3XTF32) {
+    if (t->BM != 256 || t->BN != 256)
+      return set_err(c, PF_ETILE, "3xTF32 path: the tile is 256x256 (CTA pair), got BM=%d BN=%d", t->BM, t->BN);
+    if (t->BK != 32)
+      return set_err(c, PF_ETILE, "3xTF32 path: BK must be 32 words (one 128-byte swizzle row), got %d", t->BK);
+    if (t->PAD != 0) return set_err(c, PF_ETILE, "3xTF32 path: PAD must be 0, got %d", t->PAD);
+    if (t->TN < 1 || t->TN > 64) return set_err(c, PF_ETILE, "3xTF32 path: TN (raster group) out of range: %d", t->TN);
+    if (!find_tc_variant(dt, t->BM, t->BN, t->TM, 1, &v))
+      return set_err(c, PF_ETILE, "3xTF32 path: no kernel with at most %d stages (2 or 3)", t->TM);
+    if (K % 4 != 0 || N % 4 != 0)
+      return set_err(c, PF_ESHAPE, "3xTF32 path: rows of A, B and C must be multiples of 16 bytes (N=%d, K=%d)", N, K);
+    c->group_m = t->TN;
   } else {
     return set_err(c, PF_ETILE, "dtype %d is not built in this library", (int)dt);
   }
@@ -843,13 +901,11 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
   const void *A = static_cast<const char *>(c->A) + static_cast<size_t>(r0) * c->K * e;
   void *C = static_cast<char *>(c->C) + static_cast<size_t>(r0) * c->N * o;
   if (v.path == Path::kTensor) {
-    const CUtensorMapDataType in_t =
-        (c->dtype == PF_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     CUtensorMap tmA, tmC;
     int rc;
-    if ((rc = encode_2d(c, &tmA, in_t, A, c->K, rows, c->K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (rc = encode_2d(c, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, c->N, rows, c->N * 2ull, 64, 32,
-                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    if ((rc = encode_2d(c, &tmA, in_map_type(c->dtype), A, c->K, rows, c->K * e, v.a_box_k, v.a_box_rows,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (rc = encode_c_map(c, &tmC, C, rows)))
       return rc;
     TcParams p;
     p.bias = c->bias;

@@ -209,7 +209,8 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 // Instruction descriptor of tcgen05.mma (32 bits), dense, fp32 accumulator:
 //   [4,6) D format (1 = f32)   [7,10) A format   [10,13) B format   [15] A major   [16] B major
 //   [17,23) N >> 3             [24,29) M >> 4
-// Formats: kind::f16 -> 0 = f16, 1 = bf16;  kind::f8f6f4 -> 0 = e4m3, 1 = e5m2.  Major: 0 = K, 1 = MN.
+// Formats: kind::f16 -> 0 = f16, 1 = bf16;  kind::tf32 -> 2 = tf32;  kind::f8f6f4 -> 0 = e4m3, 1 = e5m2.
+// Major: 0 = K, 1 = MN.
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t a_fmt, uint32_t b_fmt, uint32_t a_mn_major,
                                                   uint32_t b_mn_major, uint32_t M, uint32_t N) {
   return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_mn_major << 15) | (b_mn_major << 16) | ((N >> 3) << 17) |
@@ -324,6 +325,16 @@ __device__ __forceinline__ void tc_mma_f8_pair(uint32_t d_tmem, uint64_t adesc, 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Same with 32-bit operands read as TF32 (kind::tf32: 1 sign, 8 exponent, 10 mantissa bits).
+__device__ __forceinline__ void tc_mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -51,9 +51,10 @@ struct Args {
 
 pf_dtype parse_dtype(const std::string &s) {
   if (s == "f32") return PF_F32;
+  if (s == "f32_3xtf32") return PF_F32_3XTF32;
   if (s == "bf16") return PF_BF16;
   if (s == "e4m3") return PF_E4M3;
-  throw std::runtime_error("unknown dtype '" + s + "' (f32|bf16|e4m3)");
+  throw std::runtime_error("unknown dtype '" + s + "' (f32|f32_3xtf32|bf16|e4m3)");
 }
 
 B200Runner::Options runner_options(const Args &a) {

@@ -20,7 +20,7 @@ E4M3_MAX = 448.0
 @dataclass(frozen=True)
 class Workload:
     name: str
-    dtype: str          # "f32" | "bf16" | "e4m3"
+    dtype: str          # "f32" | "f32_3xtf32" | "bf16" | "e4m3"
     M: int
     N: int
     K: int
@@ -34,8 +34,8 @@ class Workload:
         return 2.0 * self.M * self.N * self.K
 
     def algorithmic_bytes(self) -> int:
-        e = {"f32": 4, "bf16": 2, "e4m3": 1}[self.dtype]
-        o = 4 if self.dtype == "f32" else 2
+        e = {"f32": 4, "f32_3xtf32": 4, "bf16": 2, "e4m3": 1}[self.dtype]
+        o = 4 if self.dtype in ("f32", "f32_3xtf32") else 2
         return self.M * self.K * e + self.K * self.N * e + self.N * 4 + self.M * self.N * o
 
 
@@ -44,6 +44,11 @@ CONFIGS = {
     "cfg1_f32_512": Workload("cfg1_f32_512", "f32", 512, 512, 512, ("uniform_sqrtk",), ("uniform_sqrtk",), 0.1, 1e-5),
     "cfg2_f32_2048": Workload("cfg2_f32_2048", "f32", 2048, 2048, 2048, ("uniform_sqrtk",), ("uniform_sqrtk",), 0.1,
                               1e-5),
+    # configs 1 and 2 again on the 3xTF32 tensor-core path (same inputs and tolerance)
+    "cfg1_f32_512_3xtf32": Workload("cfg1_f32_512_3xtf32", "f32_3xtf32", 512, 512, 512, ("uniform_sqrtk",),
+                                    ("uniform_sqrtk",), 0.1, 1e-5),
+    "cfg2_f32_2048_3xtf32": Workload("cfg2_f32_2048_3xtf32", "f32_3xtf32", 2048, 2048, 2048, ("uniform_sqrtk",),
+                                     ("uniform_sqrtk",), 0.1, 1e-5),
     "cfg3_bf16_8192": Workload("cfg3_bf16_8192", "bf16", 8192, 8192, 8192, ("normal_sqrtk",), ("normal_sqrtk",), 0.1,
                                2e-2),
     "cfg4_bf16_mlp": Workload("cfg4_bf16_mlp", "bf16", 16384, 14336, 4096, ("normal", 1.0), ("normal", 0.02), 0.02,
@@ -110,7 +115,7 @@ def make_inputs(w: Workload, seed: int = 0) -> Inputs:
     A = _draw(ra, w.a_dist, (w.M, w.K), w.K)
     B = _draw(rb, w.b_dist, (w.K, w.N), w.K)
     bias = (rbias.standard_normal(size=w.N, dtype=np.float32) * np.float32(w.bias_std)).astype(np.float32)
-    if w.dtype == "f32":
+    if w.dtype in ("f32", "f32_3xtf32"):
         return Inputs(A, B, bias, A, B)
     if w.dtype == "bf16":
         Ab, Bb = _to_bf16_bits(A), _to_bf16_bits(B)

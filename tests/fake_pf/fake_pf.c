@@ -118,6 +118,10 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
       found |= known[i][0] == t->BM && known[i][1] == t->BN && known[i][2] == t->BK && known[i][3] == t->TM &&
                known[i][4] == t->TN && known[i][5] == t->PAD;
     if (!found) return set_err(c, PF_ETILE, "fp32 tile is not compiled into this library");
+  } else if (dt == PF_F32_3XTF32) {
+    if (t->BM != 256 || t->BN != 256 || t->BK != 32 || t->PAD != 0 || t->TM < 2)
+      return set_err(c, PF_ETILE, "3xTF32 path: no kernel for this tile");
+    if (K % 4 || N % 4) return set_err(c, PF_ESHAPE, "rows must be multiples of 16 bytes");
   } else {
     return set_err(c, PF_ETILE, "dtype %d not built", (int)dt);
   }
@@ -162,7 +166,7 @@ int pf_bind(pf_ctx *c, const void *A, const void *B, const float *bias, void *C,
 }
 
 static double elem(pf_dtype dt, const void *p, size_t i) {
-  if (dt == PF_F32) return ((const float *)p)[i];
+  if (dt == PF_F32 || dt == PF_F32_3XTF32) return ((const float *)p)[i];
   if (dt == PF_BF16) {
     unsigned u = (unsigned)((const unsigned short *)p)[i] << 16;
     float f;
@@ -198,7 +202,7 @@ int pf_launch(pf_ctx *c, void *stream) {
         a += elem(c->dtype, c->A, (size_t)r * c->K + k) * elem(c->dtype, c->B, (size_t)k * c->N + j);
       const double x = a * scale + c->bias[j];
       const double y = 0.5 * x * (1.0 + tanh(0.7978845608028654 * (x + 0.044715 * x * x * x))) + wrong;
-      if (c->dtype == PF_F32)
+      if (c->dtype == PF_F32 || c->dtype == PF_F32_3XTF32)
         ((float *)c->C)[(size_t)r * c->N + j] = (float)y;
       else
         ((unsigned short *)c->C)[(size_t)r * c->N + j] = to_bf16((float)y);

@@ -1,0 +1,151 @@
+"""The fp32 path on the tensor cores (PF_F32_3XTF32), through the C ABI (needs a B200: -m gpu).
+
+Bar: the fp32 tolerance, max |ref - C| / (1 + |ref|) <= 1e-5 against fp64 (the reference gate's metric,
+core/src/cuda_runner.cpp:196), on every output at the small and BASELINE config-1/2 sizes, ragged shapes
+included, and against a plain PyTorch fp32 computation (TF32 off) at 2048^3.  The split into hi + lo must
+matter: a single TF32 product (torch with TF32 on) is at least ten times further from fp64.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from ptxforge_b200 import workloads as wl  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+DT = "f32_3xtf32"
+TILES = [(256, 256, 32, 3, 8, 0), (256, 256, 32, 2, 8, 0), (256, 256, 32, 3, 1, 0), (256, 256, 32, 8, 16, 0)]
+
+
+def operands(inp, M, N):
+    A = torch.from_numpy(np.ascontiguousarray(inp.A_raw)).cuda()
+    B = torch.from_numpy(np.ascontiguousarray(inp.B_raw)).cuda()
+    bias = torch.from_numpy(inp.bias).cuda()
+    C = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
+    return A, B, bias, C
+
+
+def run(ctx, w, inp, tile=None, ops=None):
+    A, B, bias, C = ops or operands(inp, w.M, w.N)
+    ctx.prepare(DT, tile, w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C)
+    ctx.launch(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert ctx.status() == 0
+    return C
+
+
+def full_err(oracle_mod, inp, C):
+    ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias, 1.0)
+    Cn = C.cpu().numpy()
+    assert int(np.isnan(Cn).sum()) == 0, "unwritten outputs"
+    return oracle_mod.max_rel_err(ref, Cn)
+
+
+def workload(M, N, K):
+    return wl.scaled(wl.CONFIGS["cfg1_f32_512_3xtf32"], M, N, K)
+
+
+@pytest.mark.parametrize("tile", TILES)
+def test_cfg1_every_variant(ctx, oracle_mod, tile):
+    w = wl.CONFIGS["cfg1_f32_512_3xtf32"]
+    inp = wl.make_inputs(w)
+    err = full_err(oracle_mod, inp, run(ctx, w, inp, tile))
+    assert err <= TOL, f"{tile}: {err:.3e}"
+
+
+@pytest.mark.parametrize("shape", [(200, 136, 72), (1, 8, 4), (129, 260, 36), (77, 12, 20), (300, 1000, 1000),
+                                   (513, 264, 1028)])
+def test_ragged_shapes(ctx, oracle_mod, shape):
+    w = workload(*shape)
+    inp = wl.make_inputs(w, seed=11)
+    err = full_err(oracle_mod, inp, run(ctx, w, inp))
+    assert err <= TOL, f"{shape}: {err:.3e}"
+
+
+def test_cfg2_vs_fp64_torch_fp32_and_single_tf32(ctx, oracle_mod):
+    w = wl.CONFIGS["cfg2_f32_2048_3xtf32"]
+    inp = wl.make_inputs(w)
+    A, B, bias, C = operands(inp, w.M, w.N)
+    run(ctx, w, inp, None, (A, B, bias, C))
+    err = full_err(oracle_mod, inp, C)
+    assert err <= TOL
+    gate, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, C.cpu().numpy(), samples=512, seed=99)
+    assert gate <= TOL
+    ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias, 1.0)
+
+    def err_of(allow_tf32):
+        old = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = allow_tf32
+        try:
+            x = torch.nn.functional.gelu(torch.matmul(A, B) + bias, approximate="tanh")
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = old
+        return oracle_mod.max_rel_err(ref, x.cpu().numpy())
+
+    assert err_of(False) <= TOL          # the PyTorch fp32 reference of the same op agrees
+    single = err_of(True)
+    assert err * 10 <= single, f"3xTF32 {err:.3e} vs one TF32 product {single:.3e}"
+
+
+def test_deterministic_and_close_to_the_simt_path(ctx, oracle_mod):
+    w = wl.CONFIGS["cfg2_f32_2048_3xtf32"]
+    inp = wl.make_inputs(w, seed=3)
+    ops = operands(inp, w.M, w.N)
+    first = run(ctx, w, inp, None, ops).clone()
+    again = run(ctx, w, inp, None, ops)
+    assert torch.equal(first, again)
+    simt_w = wl.CONFIGS["cfg2_f32_2048"]
+    A, B, bias, C = operands(inp, w.M, w.N)
+    ctx.prepare("f32", None, w.M, w.N, w.K)
+    ctx.bind(A, B, bias, C)
+    ctx.launch(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    d = ((first.double() - C.double()).abs() / (1 + C.double().abs())).max().item()
+    assert d <= 2 * TOL, simt_w.name
+
+
+def test_pipelined_host_path_equals_device_path(ctx):
+    w = workload(1030, 512, 256)
+    inp = wl.make_inputs(w, seed=17)
+    C = run(ctx, w, inp)
+    hC = np.empty((w.M, w.N), dtype=np.float32)
+    ctx.prepare(DT, None, w.M, w.N, w.K)
+    ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC)
+    assert np.array_equal(hC, C.cpu().numpy())
+
+
+def test_rejected_configs(ctx, pf):
+    for tile in [(128, 256, 32, 3, 8, 0), (256, 128, 32, 3, 8, 0), (256, 256, 16, 3, 8, 0), (256, 256, 32, 3, 8, 1),
+                 (256, 256, 32, 1, 8, 0)]:
+        with pytest.raises(pf.PFError) as e:
+            ctx.prepare(DT, tile, 512, 512, 512)
+        assert e.value.code == 4  # PF_ETILE
+    with pytest.raises(pf.PFError) as e:
+        ctx.prepare(DT, None, 512, 510, 512)  # rows of B / C not a multiple of 16 bytes
+    assert e.value.code == 5  # PF_ESHAPE
+    ctx.prepare(DT, None, 512, 512, 512)
+    A = torch.zeros((512, 512), device="cuda")
+    with pytest.raises(pf.PFError):
+        ctx.bind(A, A, torch.zeros(512, device="cuda"), A, 2.0, 1.0)  # scales are for e4m3 only
+
+
+def test_attrs_and_timing(ctx):
+    w = wl.CONFIGS["cfg2_f32_2048_3xtf32"]
+    inp = wl.make_inputs(w)
+    run(ctx, w, inp)
+    a = ctx.attrs()
+    assert a["threads"] == 320 and a["local_bytes"] <= 16 and a["grid"] == 2 * 64  # 8 x 8 tiles, one pair each
+    ms = ctx.time(warmup=3, iters=10, reps=3)
+    assert 0 < ms < 5.0
+    assert ctx.status() == 0
+
+
+def test_cublas_comparator_for_the_fp32_path(ctx):
+    w = wl.CONFIGS["cfg2_f32_2048_3xtf32"]
+    inp = wl.make_inputs(w)
+    run(ctx, w, inp)
+    g_ms, u_ms = ctx.time_cublas(warmup=2, iters=5, reps=3)
+    assert 0 < g_ms < u_ms

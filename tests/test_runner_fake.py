@@ -278,3 +278,16 @@ def test_ncu_counters_refuse_when_the_plain_run_fails(tune_fake, tmp_path):
     finally:
         del os.environ["FAKE_PF_FAIL_LAUNCH"]
     assert rc == 2 and not (tmp_path / "ncu_ran").exists()
+
+
+def test_fp32_3xtf32_path(tune_fake):
+    r = run(tune_fake, ["measure", "--dtype", "f32_3xtf32", "--M", "256", "--N", "256", "--K", "64", "--BM", "256",
+                        "--BN", "256", "--BK", "8", "--TM", "3", "--TN", "8", "--PAD", "4"])
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    # BK and PAD are canonicalised (32, 0) as on the tensor path; the gate is the fp32 one
+    assert r.returncode == 0 and j["ok"] and j["profile"]["max_err"] < 1e-5, j
+    r = run(tune_fake, ["measure", "--dtype", "f32_3xtf32", "--M", "256", "--N", "256", "--K", "64", *GOOD])
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 4 and "3xTF32" in j["error"]
+    g = json.loads(run(tune_fake, ["gpus", "--dtype", "f32_3xtf32"]).stdout)
+    assert g["peak_gflops"] == 375000.0
