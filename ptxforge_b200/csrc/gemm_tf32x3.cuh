@@ -16,15 +16,18 @@
 //   warp 0      TMA producer (both CTAs): its own A rows [m0 + 128*rank, +128) and B columns
 //               [n0 + 128*rank, +128) of one 32-k block (128-byte swizzled rows) into its own stage,
 //               counted on its own `full` barrier (no multicast);
-//   warps 6-9   split (both CTAs): wait for `full`, rewrite the stage in place as hi and write lo to the
-//               stage's second half (same swizzled layout, element by element), fence the writes to the
-//               async proxy and arrive on the leader's `ready` barrier (4 warps x 2 CTAs);
+//   warps 6-9   split (both CTAs): wait for `full`; A (K-major) is rewritten in place as hi with lo in
+//               the stage's second half, element by element; B arrives N-major and is written back
+//               transposed, K-major (hi in place, lo in the second half), through registers in 4 x 4
+//               blocks -- with an MN-major B operand kind::tf32 MMAs contributed nothing on this
+//               B200 (measured), K-major operands on both sides are exact; then the writes are fenced
+//               to the async proxy and each warp arrives on the leader's `ready` barrier (4 x 2 CTAs);
 //   warp 1      leader lane: waits `ready`, issues the three MMAs per 8-k step, commits the stage free
 //               (multicast to both CTAs) and the finished accumulator to both epilogues;
 //   warps 2-5   epilogue (both CTAs): tcgen05.ld 32 columns at a time, + bias[c], GELU, fp32 through a
 //               128-byte-swizzled 32 x 32 box and a TMA store; the accumulator (double-buffered, 2 x 256
 //               TMEM columns) goes back to the MMA lane right after its last load.
-// Shared memory per CTA and stage: 32 KB of hi (A 16 KB + B 16 KB) and 32 KB of lo; 3 stages.
+// Shared memory per CTA and stage: 32 KB of hi (A 16 KB + B^T 16 KB) and 32 KB of lo; 3 stages.
 #pragma once
 
 #include "gemm_tc2.cuh"
@@ -55,11 +58,11 @@ struct Tf32x3Config {
   static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 4;    // 32 rows x 128 B
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 3 * STAGES + 4 + 1;
+  static constexpr int NUM_BARS = 3 * STAGES + 4 + 1 + 1;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS + SPLIT_WARPS);
-  static constexpr uint32_t IDESC = instr_desc(2u, 2u, /*A K-major*/ 0u, /*B MN-major*/ 1u, 256, 256);
+  static constexpr uint32_t IDESC = instr_desc(2u, 2u, /*A K-major*/ 0u, /*B K-major*/ 0u, 256, 256);
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
 };
 
@@ -90,7 +93,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   uint64_t *tfull = bars + 3 * Cfg::STAGES;     // [2] both: accumulator ready
   uint64_t *tempty = tfull + 2;                 // [2] leader: both CTAs drained the accumulator
   uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *split_bar = drain + 1;              // [1] own: the 4 split warps read this stage's raw B
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(split_bar + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -113,6 +117,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       mbar_init(&tempty[a], 2 * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(split_bar, Cfg::SPLIT_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -176,8 +181,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     // ---------------------------------------------------------------- split hi / lo (warps 6..9)
     const int tid = threadIdx.x - 32 * (2 + Cfg::EPI_WARPS);
     const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready[0]), 0);
+    // B transpose: 4 k x 4 n blocks, two per thread.  Block beta -> k-block a = x ^ c, n-block
+    // b = 8m + x (c = beta / 32, m = beta / 8 % 4, x = beta % 8): in every quarter-warp the eight 16-byte
+    // reads (N-major rows) and the eight 16-byte writes (K-major rows) hit eight distinct bank groups of the
+    // 128-byte swizzle.
+    int blk_k[2], blk_n[2];
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int beta = it * 128 + tid;
+      const int x = beta & 7;
+      blk_k[it] = 4 * (x ^ (beta >> 5));
+      blk_n[it] = 4 * (8 * ((beta >> 3) & 3) + x);
+    }
     int stage = 0;
-    uint32_t phase = 0;
+    uint32_t phase = 0, split_phase = 0;
     bool ok = true;
     for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -189,8 +206,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         const uint32_t hi = smem_u32(stage_hi(stage));
         const uint32_t lo = smem_u32(stage_lo(stage));
+        // A: K-major in and out, element by element in place
 #pragma unroll 4
-        for (int i = tid; i < Cfg::RAW_BYTES / 16; i += 32 * Cfg::SPLIT_WARPS) {
+        for (int i = tid; i < Cfg::A_BYTES / 16; i += 32 * Cfg::SPLIT_WARPS) {
           uint32_t x0, x1, x2, x3;
           asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                        : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3)
@@ -202,6 +220,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
                        __float_as_uint(__uint_as_float(x2) - __uint_as_float(h2)),
                        __float_as_uint(__uint_as_float(x3) - __uint_as_float(h3)));
         }
+        // B: read this thread's two 4 x 4 blocks (N-major: chunk n/32, row k, 16-byte group (n%32/4) ^ (k%8))
+        const uint32_t braw = hi + Cfg::A_BYTES, bhi = hi + Cfg::A_BYTES, blo = lo + Cfg::A_BYTES;
+        uint32_t v[2][4][4];
+#pragma unroll
+        for (int it = 0; it < 2; ++it)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k = blk_k[it] + i, n = blk_n[it];
+            const uint32_t addr = braw + (n >> 5) * Cfg::B_CHUNK_BYTES + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4);
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[it][i][0]), "=r"(v[it][i][1]), "=r"(v[it][i][2]), "=r"(v[it][i][3])
+                         : "r"(addr));
+          }
+        // Every split warp has read the raw B before any overwrites it (bounded wait).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(split_bar);
+        const bool synced = mbar_wait(split_bar, split_phase, p.timeout_ns, abort_flag);
+        split_phase ^= 1u;
+        if (!__all_sync(0xffffffffu, synced)) {
+          if (lane == 0) fail(kErrSplitWait);
+          ok = false;
+          break;
+        }
+        // B^T: K-major rows n of 32 k, 16-byte group (k/4) ^ (n%8); hi in place, lo in the second half
+#pragma unroll
+        for (int it = 0; it < 2; ++it)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int n = blk_n[it] + j;
+            const uint32_t off = n * 128 + ((((blk_k[it] >> 2) ^ (n & 7))) << 4);
+            const uint32_t h0 = v[it][0][j] & 0xFFFFE000u, h1 = v[it][1][j] & 0xFFFFE000u,
+                           h2 = v[it][2][j] & 0xFFFFE000u, h3 = v[it][3][j] & 0xFFFFE000u;
+            st_shared_v4(bhi + off, h0, h1, h2, h3);
+            st_shared_v4(blo + off, __float_as_uint(__uint_as_float(v[it][0][j]) - __uint_as_float(h0)),
+                         __float_as_uint(__uint_as_float(v[it][1][j]) - __uint_as_float(h1)),
+                         __float_as_uint(__uint_as_float(v[it][2][j]) - __uint_as_float(h2)),
+                         __float_as_uint(__uint_as_float(v[it][3][j]) - __uint_as_float(h3)));
+          }
         // The tensor cores read shared memory through the async proxy.
         fence_proxy_async_smem();
         __syncwarp();
@@ -239,12 +295,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           const uint32_t b_hi = a_hi + Cfg::A_BYTES, b_lo = a_lo + Cfg::A_BYTES;
 #pragma unroll
           for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-            // A: K-major, k advances 32 bytes inside the swizzle row.  B: N-major, k advances 8 rows
-            // of 128 B; LBO = the next 32-column chunk.
+            // A and B^T: K-major 128-byte swizzled rows; k advances 32 bytes inside the row.
             const uint64_t ah = smem_desc(a_hi + k * 32, 16, 1024, kSwizzle128B);
             const uint64_t al = smem_desc(a_lo + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bh = smem_desc(b_hi + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
-            const uint64_t bl = smem_desc(b_lo + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+            const uint64_t bh = smem_desc(b_hi + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bl = smem_desc(b_lo + k * 32, 16, 1024, kSwizzle128B);
             // small terms first
             tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
             tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
