@@ -63,8 +63,8 @@ typedef enum {
  *                 compiled variant that fits shared memory); TN = tile-raster group height in M
  *                 blocks (consecutive tiles walk TN row blocks before moving along N); PAD = extra
  *                 128-byte k-atoms per stage (0: one atom = 64 bf16 / 128 e4m3 k, 1: two atoms).
- *   3xTF32 path : BM = BN = 256 (a CTA pair), BK = 32 (one 128-byte row of fp32 k), TM = stages
- *                 (2 or 3, clamped), TN = raster group, PAD = 0. */
+ *   3xTF32 path : BM = BN = 256 (a CTA pair), BK = 32 (one 128-byte row of fp32 k), TM = depth
+ *                 (raw TMA slots + split hi/lo slots: 2, 3 or 4, clamped), TN = raster group, PAD = 0. */
 typedef struct {
   int BM, BN, BK, TM, TN, PAD;
 } pf_tile;

@@ -56,10 +56,10 @@ class Attr(ctypes.Structure):
 # Best-measured defaults per dtype.  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
 # stage (PAD=1) and as many stages as fit (TM=8 -> 3), raster group 8 M-blocks (TN=8) -- the lowest energy
 # per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4; 3xTF32: CTA pair,
-# 3 stages, raster group 8.
+# 2 raw + 2 split slots (depth 4), raster group 8.
 DEFAULT_TILES = {
     "f32": (128, 128, 8, 8, 8, 4),
-    "f32_3xtf32": (256, 256, 32, 3, 8, 0),
+    "f32_3xtf32": (256, 256, 32, 4, 8, 0),
     "bf16": (256, 256, 32, 8, 8, 1),
     "e4m3": (256, 256, 32, 8, 8, 1),
 }

@@ -9,38 +9,44 @@
 //     lo = x - hi                                     (exact in fp32, |lo| < 2^-10 |x|)
 // and a*b is accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b (tcgen05.mma kind::tf32, fp32 in TMEM).
 // The dropped lo_a*lo_b term is below 2^-20 |a*b| and the TF32 reading of lo loses at most 2^-21 |x|,
-// so each product is good to ~2^-19 relative -- inside the fp32 path's 1e-5 tolerance, with the
-// epilogue's GELU in the reference's own form (tanhf), not the MUFU approximation of the bf16 path.
+// so each product is good to ~2^-19 relative -- inside the fp32 path's 1e-5 tolerance.  The epilogue's
+// GELU is the reference's function evaluated through 1 + tanh(u) = 2 / (1 + e^-2u) (see gelu_tanh_exp).
 //
-// CTA pairs (cluster of 2, tcgen05 .cta_group::2, M = 256, N = 256), persistent, 320 threads per CTA:
-//   warp 0      TMA producer (both CTAs): its own A rows [m0 + 128*rank, +128) and B columns
-//               [n0 + 128*rank, +128) of one 32-k block (128-byte swizzled rows) into its own stage,
-//               counted on its own `full` barrier (no multicast);
-//   warps 6-9   split (both CTAs): wait for `full`; A (K-major) is rewritten in place as hi with lo in
-//               the stage's second half, element by element; B arrives N-major and is written back
-//               transposed, K-major (hi in place, lo in the second half), through registers in 4 x 4
-//               blocks -- with an MN-major B operand kind::tf32 MMAs contributed nothing on this
-//               B200 (measured), K-major operands on both sides are exact; then the writes are fenced
-//               to the async proxy and each warp arrives on the leader's `ready` barrier (4 x 2 CTAs);
-//   warp 1      leader lane: waits `ready`, issues the three MMAs per 8-k step, commits the stage free
+// CTA pairs (cluster of 2, tcgen05 .cta_group::2, M = 256, N = 256), persistent, 448 threads per CTA, and
+// two shared-memory rings per CTA:
+//   raw ring   (RAW_STAGES x 32 KB): what TMA brings in -- A rows [m0 + 128*rank, +128) K-major and B
+//              columns [n0 + 128*rank, +128) N-major, one 32-k block each;
+//   split ring (SPLIT_STAGES x 64 KB): the MMA operands -- A hi | A lo | B^T hi | B^T lo, all K-major.
+// Roles:
+//   warp 0      TMA producer (both CTAs): fills the raw ring, counted on its own `raw_full` barrier (no
+//               multicast), as soon as the split warps have taken a slot's data into registers;
+//   warps 6-13  split (both CTAs): raw slot -> registers (A 16-byte runs; B in 4 x 4 blocks) -> release the
+//               raw slot -> hi / lo -> split slot, B written back transposed (K-major); fence to the async
+//               proxy; arrive on the leader's `ready` barrier (8 warps x 2 CTAs).  B must be transposed:
+//               with an MN-major B operand kind::tf32 MMAs contributed nothing on this B200 (measured),
+//               K-major operands on both sides are exact;
+//   warp 1      leader lane: waits `ready`, issues the three MMAs per 8-k step, commits the split slot free
 //               (multicast to both CTAs) and the finished accumulator to both epilogues;
 //   warps 2-5   epilogue (both CTAs): tcgen05.ld 32 columns at a time, + bias[c], GELU, fp32 through a
 //               128-byte-swizzled 32 x 32 box and a TMA store; the accumulator (double-buffered, 2 x 256
 //               TMEM columns) goes back to the MMA lane right after its last load.
-// Shared memory per CTA and stage: 32 KB of hi (A 16 KB + B^T 16 KB) and 32 KB of lo; 3 stages.
+// Separate rings let TMA run ahead of the MMAs (a raw slot is free once split, not once multiplied) and
+// let the split write without waiting for its own reads of the slot to finish elsewhere in the block.
 #pragma once
 
 #include "gemm_tc2.cuh"
 
 namespace pf {
 
-template <int kStages>
+template <int kRawStages, int kSplitStages>
 struct Tf32x3Config {
   static constexpr int BM = 256;                             // pair tile rows
   static constexpr int BM_CTA = 128;
   static constexpr int BN = 256;                             // pair tile columns (UMMA N)
   static constexpr int BN_CTA = 128;                         // B columns loaded by each CTA
-  static constexpr int STAGES = kStages;
+  static constexpr int RAW_STAGES = kRawStages;
+  static constexpr int SPLIT_STAGES = kSplitStages;
+  static constexpr int STAGES = kRawStages + kSplitStages;   // pipeline depth reported to the host
   static constexpr int ELEM = 4;
   static constexpr int ATOM_K = 32;                          // fp32 elements in one 128-byte row
   static constexpr int BK = ATOM_K;                          // k per stage
@@ -49,18 +55,19 @@ struct Tf32x3Config {
   static constexpr int B_CHUNK_N = 32;                       // N elements per 128-byte row of B
   static constexpr int B_CHUNKS = BN_CTA / B_CHUNK_N;
   static constexpr int B_CHUNK_BYTES = BK * 128;
-  static constexpr int B_BYTES = B_CHUNKS * B_CHUNK_BYTES;
-  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;        // what TMA brings in (then hi, in place)
-  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;          // hi + lo
+  static constexpr int B_BYTES = B_CHUNKS * B_CHUNK_BYTES;   // = BN_CTA rows x 128 B once transposed
+  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;        // one raw slot
+  static constexpr int SPLIT_BYTES = 2 * RAW_BYTES;          // one split slot: A hi, A lo, B^T hi, B^T lo
   static constexpr int EPI_WARPS = 4;
-  static constexpr int SPLIT_WARPS = 4;
+  static constexpr int SPLIT_WARPS = 8;
   static constexpr int EPI_COLS = 32;                        // fp32 columns per TMA store box (128 B)
   static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 4;    // 32 rows x 128 B
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 3 * STAGES + 4 + 1 + 1;
+  static constexpr int NUM_BARS = 2 * RAW_STAGES + 2 * SPLIT_STAGES + 4 + 1;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int SMEM_BYTES =
+      1024 + SPLIT_STAGES * SPLIT_BYTES + RAW_STAGES * RAW_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS + SPLIT_WARPS);
   static constexpr uint32_t IDESC = instr_desc(2u, 2u, /*A K-major*/ 0u, /*B K-major*/ 0u, 256, 256);
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
@@ -68,10 +75,30 @@ struct Tf32x3Config {
 
 enum : unsigned { kErrSplitWait = 16u };
 
-// 0.5*x*(1 + tanh(k0*(x + k1*x^3))) as the reference writes it (kernels/gemm_bias_gelu.cu:37-40).
-__device__ __forceinline__ float gelu_tanh_f32(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+// The reference's GELU, 0.5*x*(1 + tanh(u)) with u = k0*(x + k1*x^3) (kernels/gemm_bias_gelu.cu:37-40),
+// rewritten with 1 + tanh(u) = 2 / (1 + e^-2u) as x / (1 + e^-2u).  __expf and __fdividef (the hardware
+// exponential and reciprocal) keep it within ~1e-6 relative of the fp64 function over the whole range
+// (e^-2u overflowing to +inf for very negative x gives the right limit, -0), inside the fp32 path's 1e-5
+// and far cheaper than tanhf in an epilogue that a single-tile-per-pair launch cannot hide.
+__device__ __forceinline__ float gelu_tanh_exp(float x) {
+  const float k0 = 0.7978845608028654f, k0k1 = 0.7978845608028654f * 0.044715f;
+  const float u = x * fmaf(k0k1, x * x, k0);
+  return __fdividef(x, 1.0f + __expf(-2.0f * u));
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+// hi (TF32: low 13 mantissa bits cleared) and lo = x - hi of four fp32 words, stored at hi_addr / lo_addr.
+__device__ __forceinline__ void store_split4(uint32_t hi_addr, uint32_t lo_addr, uint32_t x0, uint32_t x1, uint32_t x2,
+                                             uint32_t x3) {
+  const uint32_t h0 = x0 & 0xFFFFE000u, h1 = x1 & 0xFFFFE000u, h2 = x2 & 0xFFFFE000u, h3 = x3 & 0xFFFFE000u;
+  st_shared_v4(hi_addr, h0, h1, h2, h3);
+  st_shared_v4(lo_addr, __float_as_uint(__uint_as_float(x0) - __uint_as_float(h0)),
+               __float_as_uint(__uint_as_float(x1) - __uint_as_float(h1)),
+               __float_as_uint(__uint_as_float(x2) - __uint_as_float(h2)),
+               __float_as_uint(__uint_as_float(x3) - __uint_as_float(h3)));
 }
 
 template <class Cfg>
@@ -82,19 +109,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
-  // stage s: [hi A | hi B | lo A | lo B], each half RAW_BYTES, all 1024-byte aligned
-  auto stage_hi = [&](int s) { return smem + s * Cfg::STAGE_BYTES; };
-  auto stage_lo = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_BYTES; };
-  uint8_t *sEpi = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  // split slot s: [A hi | A lo | B^T hi | B^T lo] (16 KB each); raw slot r: [A | B]; all 1024-byte aligned
+  uint8_t *sSplit = smem;
+  uint8_t *sRaw = smem + Cfg::SPLIT_STAGES * Cfg::SPLIT_BYTES;
+  uint8_t *sEpi = sRaw + Cfg::RAW_STAGES * Cfg::RAW_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + Cfg::EPI_BYTES);
-  uint64_t *full = bars;                        // [STAGES] own: this CTA's TMA bytes landed
-  uint64_t *ready = bars + Cfg::STAGES;         // [STAGES] leader: both CTAs' stages split
-  uint64_t *empty = bars + 2 * Cfg::STAGES;     // [STAGES] both: MMAs reading the stage finished
-  uint64_t *tfull = bars + 3 * Cfg::STAGES;     // [2] both: accumulator ready
-  uint64_t *tempty = tfull + 2;                 // [2] leader: both CTAs drained the accumulator
-  uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
-  uint64_t *split_bar = drain + 1;              // [1] own: the 4 split warps read this stage's raw B
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(split_bar + 1);
+  uint64_t *raw_full = bars;                              // [RAW] own: TMA bytes landed
+  uint64_t *raw_empty = raw_full + Cfg::RAW_STAGES;       // [RAW] own: the split warps took the data
+  uint64_t *ready = raw_empty + Cfg::RAW_STAGES;          // [SPLIT] leader: both CTAs' split slot written
+  uint64_t *split_empty = ready + Cfg::SPLIT_STAGES;      // [SPLIT] both: the MMAs reading the slot finished
+  uint64_t *tfull = split_empty + Cfg::SPLIT_STAGES;      // [2] both: accumulator ready
+  uint64_t *tempty = tfull + 2;                           // [2] leader: both CTAs drained the accumulator
+  uint64_t *drain = tempty + 2;                           // [1] leader: all MMAs complete
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -107,17 +134,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
-    for (int s = 0; s < Cfg::STAGES; ++s) {
-      mbar_init(&full[s], 1);
+    for (int r = 0; r < Cfg::RAW_STAGES; ++r) {
+      mbar_init(&raw_full[r], 1);
+      mbar_init(&raw_empty[r], Cfg::SPLIT_WARPS);
+    }
+    for (int s = 0; s < Cfg::SPLIT_STAGES; ++s) {
       mbar_init(&ready[s], 2 * Cfg::SPLIT_WARPS);
-      mbar_init(&empty[s], 1);
+      mbar_init(&split_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
-    mbar_init(split_bar, Cfg::SPLIT_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -139,7 +168,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
-      int stage = 0;
+      int slot = 0;
       uint32_t phase = 0;
       bool ok = true;
       int issued = 0;
@@ -149,130 +178,124 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
+          if (!mbar_wait(&raw_empty[slot], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
             break;
           }
-          uint8_t *dst = stage_hi(stage);
-          mbar_arrive_expect_tx(&full[stage], Cfg::RAW_BYTES);
-          tma_load_2d(dst, &tmA, &full[stage], kb * Cfg::BK, m0);
+          uint8_t *dst = sRaw + slot * Cfg::RAW_BYTES;
+          mbar_arrive_expect_tx(&raw_full[slot], Cfg::RAW_BYTES);
+          tma_load_2d(dst, &tmA, &raw_full[slot], kb * Cfg::BK, m0);
 #pragma unroll
           for (int j = 0; j < Cfg::B_CHUNKS; ++j)
-            tma_load_2d(dst + Cfg::A_BYTES + j * Cfg::B_CHUNK_BYTES, &tmB, &full[stage], n0 + j * Cfg::B_CHUNK_N,
+            tma_load_2d(dst + Cfg::A_BYTES + j * Cfg::B_CHUNK_BYTES, &tmB, &raw_full[slot], n0 + j * Cfg::B_CHUNK_N,
                         kb * Cfg::BK);
           ++issued;
-          if (++stage == Cfg::STAGES) {
-            stage = 0;
+          if (++slot == Cfg::RAW_STAGES) {
+            slot = 0;
             phase ^= 1u;
           }
         }
       }
       if (!ok) {
         // Loads already issued land before the block may exit (bounded).
-        for (int s = 0; s < Cfg::STAGES && s < issued; ++s) {
-          const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+        for (int r = 0; r < Cfg::RAW_STAGES && r < issued; ++r) {
+          const uint32_t ph = (r < slot) ? phase : (phase ^ 1u);
           volatile int no_abort = 0;
-          if (!mbar_wait(&full[s], ph, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+          if (!mbar_wait(&raw_full[r], ph, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
         }
       }
     }
   } else if (warp >= 2 + Cfg::EPI_WARPS) {
-    // ---------------------------------------------------------------- split hi / lo (warps 6..9)
+    // ---------------------------------------------------------------- split hi / lo (warps 6..13)
+    constexpr int SPLIT_THREADS = 32 * Cfg::SPLIT_WARPS;
+    constexpr int A_VEC = Cfg::A_BYTES / 16 / SPLIT_THREADS;   // 16-byte runs of A per thread
+    constexpr int BLOCKS = 256 / SPLIT_THREADS;                // 4 x 4 blocks of B per thread
+    static_assert(A_VEC * SPLIT_THREADS * 16 == Cfg::A_BYTES && BLOCKS * SPLIT_THREADS == 256,
+                  "split threads must divide the A runs and the 256 transpose blocks");
     const int tid = threadIdx.x - 32 * (2 + Cfg::EPI_WARPS);
     const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready[0]), 0);
-    // B transpose: 4 k x 4 n blocks, two per thread.  Block beta -> k-block a = x ^ c, n-block
-    // b = 8m + x (c = beta / 32, m = beta / 8 % 4, x = beta % 8): in every quarter-warp the eight 16-byte
-    // reads (N-major rows) and the eight 16-byte writes (K-major rows) hit eight distinct bank groups of the
-    // 128-byte swizzle.
-    int blk_k[2], blk_n[2];
+    // B transpose: block beta -> k-block a = x ^ c, n-block b = 8m + x (c = beta / 32, m = beta / 8 % 4,
+    // x = beta % 8): in every quarter-warp the eight 16-byte reads (N-major rows) and the eight 16-byte
+    // writes (K-major rows) hit eight distinct bank groups of the 128-byte swizzle.
+    int blk_k[BLOCKS], blk_n[BLOCKS];
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int beta = it * 128 + tid;
+    for (int it = 0; it < BLOCKS; ++it) {
+      const int beta = it * SPLIT_THREADS + tid;
       const int x = beta & 7;
       blk_k[it] = 4 * (x ^ (beta >> 5));
       blk_n[it] = 4 * (8 * ((beta >> 3) & 3) + x);
     }
-    int stage = 0;
-    uint32_t phase = 0, split_phase = 0;
+    int rslot = 0, sslot = 0;
+    uint32_t rphase = 0, sphase = 0;
     bool ok = true;
     for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
-        const bool waited = mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag);
+        // 1. the raw slot's bytes, into registers
+        bool waited = mbar_wait(&raw_full[rslot], rphase, p.timeout_ns, abort_flag);
         if (!__all_sync(0xffffffffu, waited)) {
           if (lane == 0) fail(kErrSplitWait);
           ok = false;
           break;
         }
-        const uint32_t hi = smem_u32(stage_hi(stage));
-        const uint32_t lo = smem_u32(stage_lo(stage));
-        // A: K-major in and out, element by element in place
-#pragma unroll 4
-        for (int i = tid; i < Cfg::A_BYTES / 16; i += 32 * Cfg::SPLIT_WARPS) {
-          uint32_t x0, x1, x2, x3;
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3)
-                       : "r"(hi + i * 16));
-          const uint32_t h0 = x0 & 0xFFFFE000u, h1 = x1 & 0xFFFFE000u, h2 = x2 & 0xFFFFE000u, h3 = x3 & 0xFFFFE000u;
-          st_shared_v4(hi + i * 16, h0, h1, h2, h3);
-          st_shared_v4(lo + i * 16, __float_as_uint(__uint_as_float(x0) - __uint_as_float(h0)),
-                       __float_as_uint(__uint_as_float(x1) - __uint_as_float(h1)),
-                       __float_as_uint(__uint_as_float(x2) - __uint_as_float(h2)),
-                       __float_as_uint(__uint_as_float(x3) - __uint_as_float(h3)));
-        }
-        // B: read this thread's two 4 x 4 blocks (N-major: chunk n/32, row k, 16-byte group (n%32/4) ^ (k%8))
-        const uint32_t braw = hi + Cfg::A_BYTES, bhi = hi + Cfg::A_BYTES, blo = lo + Cfg::A_BYTES;
-        uint32_t v[2][4][4];
+        const uint32_t ra = smem_u32(sRaw + rslot * Cfg::RAW_BYTES), rb = ra + Cfg::A_BYTES;
+        uint32_t a[A_VEC][4];
 #pragma unroll
-        for (int it = 0; it < 2; ++it)
+        for (int i = 0; i < A_VEC; ++i) ld_shared_v4(ra + (tid + i * SPLIT_THREADS) * 16, a[i]);
+        uint32_t v[BLOCKS][4][4];  // N-major: chunk n/32, row k, 16-byte group (n%32/4) ^ (k%8)
+#pragma unroll
+        for (int it = 0; it < BLOCKS; ++it)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int k = blk_k[it] + i, n = blk_n[it];
-            const uint32_t addr = braw + (n >> 5) * Cfg::B_CHUNK_BYTES + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4);
-            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(v[it][i][0]), "=r"(v[it][i][1]), "=r"(v[it][i][2]), "=r"(v[it][i][3])
-                         : "r"(addr));
+            ld_shared_v4(rb + (n >> 5) * Cfg::B_CHUNK_BYTES + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4), v[it][i]);
           }
-        // Every split warp has read the raw B before any overwrites it (bounded wait).
+        // 2. the raw slot goes back to the producer once every lane of the warp holds its data
         __syncwarp();
-        if (lane == 0) mbar_arrive(split_bar);
-        const bool synced = mbar_wait(split_bar, split_phase, p.timeout_ns, abort_flag);
-        split_phase ^= 1u;
-        if (!__all_sync(0xffffffffu, synced)) {
+        if (lane == 0) mbar_arrive(&raw_empty[rslot]);
+        if (++rslot == Cfg::RAW_STAGES) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        // 3. hi / lo into the split slot, once the MMAs have released it
+        waited = mbar_wait(&split_empty[sslot], sphase ^ 1u, p.timeout_ns, abort_flag);
+        if (!__all_sync(0xffffffffu, waited)) {
           if (lane == 0) fail(kErrSplitWait);
           ok = false;
           break;
         }
-        // B^T: K-major rows n of 32 k, 16-byte group (k/4) ^ (n%8); hi in place, lo in the second half
+        const uint32_t s0 = smem_u32(sSplit + sslot * Cfg::SPLIT_BYTES);
+        const uint32_t a_hi = s0, a_lo = s0 + Cfg::A_BYTES, b_hi = s0 + 2 * Cfg::A_BYTES,
+                       b_lo = b_hi + Cfg::B_BYTES;
 #pragma unroll
-        for (int it = 0; it < 2; ++it)
+        for (int i = 0; i < A_VEC; ++i) {
+          const uint32_t off = (tid + i * SPLIT_THREADS) * 16;
+          store_split4(a_hi + off, a_lo + off, a[i][0], a[i][1], a[i][2], a[i][3]);
+        }
+        // B^T: K-major rows n of 32 k, 16-byte group (k/4) ^ (n%8)
+#pragma unroll
+        for (int it = 0; it < BLOCKS; ++it)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int n = blk_n[it] + j;
-            const uint32_t off = n * 128 + ((((blk_k[it] >> 2) ^ (n & 7))) << 4);
-            const uint32_t h0 = v[it][0][j] & 0xFFFFE000u, h1 = v[it][1][j] & 0xFFFFE000u,
-                           h2 = v[it][2][j] & 0xFFFFE000u, h3 = v[it][3][j] & 0xFFFFE000u;
-            st_shared_v4(bhi + off, h0, h1, h2, h3);
-            st_shared_v4(blo + off, __float_as_uint(__uint_as_float(v[it][0][j]) - __uint_as_float(h0)),
-                         __float_as_uint(__uint_as_float(v[it][1][j]) - __uint_as_float(h1)),
-                         __float_as_uint(__uint_as_float(v[it][2][j]) - __uint_as_float(h2)),
-                         __float_as_uint(__uint_as_float(v[it][3][j]) - __uint_as_float(h3)));
+            const uint32_t off = n * 128 + (((blk_k[it] >> 2) ^ (n & 7)) << 4);
+            store_split4(b_hi + off, b_lo + off, v[it][0][j], v[it][1][j], v[it][2][j], v[it][3][j]);
           }
         // The tensor cores read shared memory through the async proxy.
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(ready_leader0 + stage * 8);
-        if (++stage == Cfg::STAGES) {
-          stage = 0;
-          phase ^= 1u;
+        if (lane == 0) mbar_arrive_cluster(ready_leader0 + sslot * 8);
+        if (++sslot == Cfg::SPLIT_STAGES) {
+          sslot = 0;
+          sphase ^= 1u;
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int sslot = 0;
+      uint32_t sphase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
@@ -285,14 +308,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait_cluster(&ready[stage], phase, p.timeout_ns, abort_flag)) {
+          if (!mbar_wait_cluster(&ready[sslot], sphase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_hi = smem_u32(stage_hi(stage)), a_lo = smem_u32(stage_lo(stage));
-          const uint32_t b_hi = a_hi + Cfg::A_BYTES, b_lo = a_lo + Cfg::A_BYTES;
+          const uint32_t a_hi = smem_u32(sSplit + sslot * Cfg::SPLIT_BYTES), a_lo = a_hi + Cfg::A_BYTES;
+          const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
 #pragma unroll
           for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
             // A and B^T: K-major 128-byte swizzled rows; k advances 32 bytes inside the row.
@@ -305,10 +328,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
             tc_mma_tf32_pair(d_tmem, ah, bh, Cfg::IDESC, 1u);
           }
-          tc_commit_pair_mc(&empty[stage], 0x3);
-          if (++stage == Cfg::STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          tc_commit_pair_mc(&split_empty[sslot], 0x3);
+          if (++sslot == Cfg::SPLIT_STAGES) {
+            sslot = 0;
+            sphase ^= 1u;
           }
         }
         if (!ok) break;
@@ -359,10 +382,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         for (int j4 = 0; j4 < 8; ++j4) {
           float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
           if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
-          const float y0 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 0]) + b4.x);
-          const float y1 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 1]) + b4.y);
-          const float y2 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 2]) + b4.z);
-          const float y3 = gelu_tanh_f32(__uint_as_float(v[j4 * 4 + 3]) + b4.w);
+          const float y0 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 0]) + b4.x);
+          const float y1 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 1]) + b4.y);
+          const float y2 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 2]) + b4.z);
+          const float y3 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 3]) + b4.w);
           // row `lane` of the 32 x 32 fp32 box: 16-byte chunk j4 goes to chunk j4 ^ (row % 8)
           st_shared_v4(sbuf + static_cast<uint32_t>((j4 ^ (lane & 7)) * 16), __float_as_uint(y0), __float_as_uint(y1),
                        __float_as_uint(y2), __float_as_uint(y3));

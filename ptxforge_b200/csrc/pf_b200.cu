@@ -123,16 +123,17 @@ Variant make_tc2_variant() {
   return v;
 }
 
-template <int ST>
+template <int RAW, int SPLIT>
 void launch_tf32x3_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                         const TcParams &p) {
-  using Cfg = pf::Tf32x3Config<ST>;
+  using Cfg = pf::Tf32x3Config<RAW, SPLIT>;
   pf::gemm_bias_gelu_tf32x3<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
 }
 
-template <int ST>
+// 3xTF32: depth = raw TMA slots + split (hi / lo) slots.
+template <int RAW, int SPLIT>
 Variant make_tf32x3_variant() {
-  using Cfg = pf::Tf32x3Config<ST>;
+  using Cfg = pf::Tf32x3Config<RAW, SPLIT>;
   Variant v;
   v.path = Path::kTensor;
   v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tf32x3<Cfg>);
@@ -148,7 +149,7 @@ Variant make_tf32x3_variant() {
   v.a_box_k = Cfg::ATOM_K;
   v.katoms = 1;
   v.cta_per_tile = 2;
-  v.launch_tc = &launch_tf32x3_impl<ST>;
+  v.launch_tc = &launch_tf32x3_impl<RAW, SPLIT>;
   return v;
 }
 
@@ -219,7 +220,9 @@ bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant
       {PF_E4M3, 128, 128, 6, 1, &make_tc_variant<1, 128, 6>},     {PF_E4M3, 256, 256, 2, 1, &make_tc2_variant<1, 2>},
       {PF_E4M3, 256, 256, 4, 1, &make_tc2_variant<1, 4>},         {PF_E4M3, 256, 256, 6, 1, &make_tc2_variant<1, 6>},
       {PF_E4M3, 256, 256, 3, 2, &make_tc2_variant<1, 3, 2>},
-      {PF_F32_3XTF32, 256, 256, 2, 1, &make_tf32x3_variant<2>}, {PF_F32_3XTF32, 256, 256, 3, 1, &make_tf32x3_variant<3>},
+      {PF_F32_3XTF32, 256, 256, 2, 1, &make_tf32x3_variant<1, 1>},
+      {PF_F32_3XTF32, 256, 256, 3, 1, &make_tf32x3_variant<1, 2>},
+      {PF_F32_3XTF32, 256, 256, 4, 1, &make_tf32x3_variant<2, 2>},
   };
   const Entry *best = nullptr;
   for (const Entry &e : table)
@@ -703,7 +706,7 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     if (t->PAD != 0) return set_err(c, PF_ETILE, "3xTF32 path: PAD must be 0, got %d", t->PAD);
     if (t->TN < 1 || t->TN > 64) return set_err(c, PF_ETILE, "3xTF32 path: TN (raster group) out of range: %d", t->TN);
     if (!find_tc_variant(dt, t->BM, t->BN, t->TM, 1, &v))
-      return set_err(c, PF_ETILE, "3xTF32 path: no kernel with at most %d stages (2 or 3)", t->TM);
+      return set_err(c, PF_ETILE, "3xTF32 path: no kernel with at most %d stages (2 to 4)", t->TM);
     if (K % 4 != 0 || N % 4 != 0)
       return set_err(c, PF_ESHAPE, "3xTF32 path: rows of A, B and C must be multiples of 16 bytes (N=%d, K=%d)", N, K);
     c->group_m = t->TN;

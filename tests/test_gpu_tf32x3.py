@@ -16,7 +16,8 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-5
 DT = "f32_3xtf32"
-TILES = [(256, 256, 32, 3, 8, 0), (256, 256, 32, 2, 8, 0), (256, 256, 32, 3, 1, 0), (256, 256, 32, 8, 16, 0)]
+TILES = [(256, 256, 32, 4, 8, 0), (256, 256, 32, 3, 8, 0), (256, 256, 32, 2, 8, 0), (256, 256, 32, 4, 1, 0),
+         (256, 256, 32, 8, 16, 0)]
 
 
 def operands(inp, M, N):
@@ -137,7 +138,7 @@ def test_attrs_and_timing(ctx):
     inp = wl.make_inputs(w)
     run(ctx, w, inp)
     a = ctx.attrs()
-    assert a["threads"] == 320 and a["local_bytes"] <= 16 and a["grid"] == 2 * 64  # 8 x 8 tiles, one pair each
+    assert a["threads"] == 448 and a["local_bytes"] <= 16 and a["grid"] == 2 * 64  # 8 x 8 tiles, one pair each
     ms = ctx.time(warmup=3, iters=10, reps=3)
     assert 0 < ms < 5.0
     assert ctx.status() == 0
