@@ -233,7 +233,7 @@ def run_ours(args, dist):
     r0, rows = pf.shard_rows(w.M, dist.world, dist.rank, 128)
     A, B, bias, C = device_operands(torch, w, inp, r0, rows)
     scale = inp.scale_a * inp.scale_b
-    tile = tuple(int(x) for x in args.tile.split(",")) if args.tile else pf.DEFAULT_TILES[w.dtype]
+    tile = tuple(int(x) for x in args.tile.split(",")) if args.tile else pf.default_tile(w.dtype, rows, w.N)
     ctx = pf.Context(dist.local_rank)
     ctx.prepare(w.dtype, tile, rows, w.N, w.K)
     ctx.bind(A, B, bias, C, inp.scale_a, inp.scale_b)

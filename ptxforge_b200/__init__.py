@@ -65,6 +65,25 @@ DEFAULT_TILES = {
 }
 
 
+def default_tile(dtype: str, rows: int, N: int, pairs: int = 74) -> tuple:
+    """The best-measured tile for a rows x N output on one GPU.
+
+    bf16 / e4m3 use CTA-pair tiles 256 rows high, 256 or 224 columns wide: the time of a launch is about the
+    number of waves of tiles over the resident pairs times the tile width, and 224-wide tiles fill whole waves
+    where 256-wide ones leave a partial last wave (8192 columns on 1024- or 2048-row shards: 37 x 224 columns
+    make 148 / 296 tiles = 2 / 4 full waves of 74 pairs).  Ties keep 256.
+    """
+    base = DEFAULT_TILES[dtype]
+    if dtype not in ("bf16", "e4m3") or base[0] != 256:
+        return base
+
+    def cost(bn):
+        tiles = -(-rows // 256) * -(-N // bn)
+        return -(-tiles // pairs) * bn
+
+    return base[:1] + (224,) + base[2:] if cost(224) < cost(256) else base
+
+
 class PFError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"{ERROR_NAMES.get(code, code)}: {msg}")

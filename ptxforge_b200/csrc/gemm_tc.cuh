@@ -115,19 +115,40 @@ struct NoAddend {
   __device__ __forceinline__ void operator()(uint32_t (&)[32], int) const {}
 };
 
+// 32 accumulator columns of one row (this lane's) -> x*scale + bias[c], GELU -> 16 packed bf16 pairs.
+__device__ __forceinline__ void epilogue_math32(const uint32_t (&v)[32], int n0, const TcParams &p,
+                                                uint32_t (&packed)[16]) {
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
+    const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
+    const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
+    const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
+    const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
+    packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
+    packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
+  }
+}
+
 // One epilogue warp turns its 32 accumulator rows x BN columns (TMEM lanes q*32.., columns from
 // `t_row`) into C rows [m0, m0+32) x columns [n_tile, n_tile+BN): x*scale + bias[c], GELU, bf16,
-// staged through a double-buffered 32 x 64 swizzled shared-memory box and TMA-stored.
+// staged through a double-buffered 32 x 64 swizzled shared-memory box and TMA-stored (`tmC`, 64 x 32
+// boxes, 128-byte swizzle).  A BN that is 32 past a multiple of 64 ends with one 32-column box through
+// `tmC_tail` (32 x 32 boxes, 64-byte swizzle), so a tile never writes into its neighbour's columns.
 // `release()` is called by the whole warp right after the last TMEM load of the tile; `addend(v, c0)`
 // may add other fp32 contributions to accumulator columns [c0, c0+32) before the epilogue math.
 template <int BN, class Release, class Addend = NoAddend>
 __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile, const TcParams &p,
-                                              const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
-                                              Release release, Addend addend = Addend()) {
+                                              const CUtensorMap *tmC, const CUtensorMap *tmC_tail, uint8_t *ebuf,
+                                              int &buf, int lane, Release release, Addend addend = Addend()) {
   constexpr int EPI_COLS = 64;
   constexpr int BUF_BYTES = 32 * EPI_COLS * 2;
+  constexpr int FULL = BN / EPI_COLS;
+  constexpr bool TAIL = (BN % EPI_COLS) != 0;
+  static_assert(BN % 32 == 0, "the epilogue works in 32-column steps");
 #pragma unroll 1
-  for (int c = 0; c < BN / EPI_COLS; ++c) {
+  for (int c = 0; c < FULL; ++c) {
     const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 128;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -135,19 +156,8 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
       tmem_ld_32x32b_x32(t_row + c * EPI_COLS + h * 32, v);
       tmem_ld_wait();
       addend(v, c * EPI_COLS + h * 32);
-      const int n0 = n_tile + c * EPI_COLS + h * 32;
       uint32_t packed[16];
-#pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
-        const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
-        const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
-        const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
-        const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
-        packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
-        packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
-      }
+      epilogue_math32(v, n_tile + c * EPI_COLS + h * 32, p, packed);
       // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -155,7 +165,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
         st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2], packed[i * 4 + 3]);
       }
     }
-    if (c == BN / EPI_COLS - 1) {
+    if (!TAIL && c == FULL - 1) {
       // Last TMEM read of this accumulator: hand it back to the MMA issuer.
       tc_fence_before();
       __syncwarp();
@@ -167,6 +177,34 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
       tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n_tile + c * EPI_COLS, m0);
       tma_store_commit();
       tma_store_wait_read<1>();  // the other buffer is free again
+    }
+    __syncwarp();
+    buf ^= 1;
+  }
+  if constexpr (TAIL) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(t_row + FULL * EPI_COLS, v);
+    tmem_ld_wait();
+    tc_fence_before();
+    __syncwarp();
+    release();
+    addend(v, FULL * EPI_COLS);
+    uint32_t packed[16];
+    epilogue_math32(v, n_tile + FULL * EPI_COLS, p, packed);
+    // Row `lane` of the 32 x 32 box is 64 bytes; under the 64-byte swizzle its 16-byte chunk i lands at
+    // chunk i ^ ((row / 2) % 4), which also spreads a quarter-warp's stores over all eight bank groups.
+    const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 64;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t chunk = static_cast<uint32_t>(i ^ ((lane >> 1) & 3));
+      st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2], packed[i * 4 + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC_tail, ebuf + buf * BUF_BYTES, n_tile + FULL * EPI_COLS, m0);
+      tma_store_commit();
+      tma_store_wait_read<1>();
     }
     __syncwarp();
     buf ^= 1;
@@ -347,7 +385,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int m0 = mb * Cfg::BM + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
       uint64_t *tempty_acc = &tempty[acc];
-      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, ebuf, buf, lane, [&] {
+      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, nullptr, ebuf, buf, lane, [&] {
         if (lane == 0) mbar_arrive(tempty_acc);
       });
       if (++acc == 2) {

@@ -27,12 +27,14 @@
 
 namespace pf {
 
-template <int kDtype, int kStages, int kKAtoms = 1>
+// kBN: pair tile columns (UMMA N), 256 or 224.  A 224-wide tile gives 37 column tiles for N = 8192, so
+// row shards whose 256-wide tiles would leave a partial last wave fill whole waves of pairs instead.
+template <int kDtype, int kStages, int kKAtoms = 1, int kBN = 256>
 struct Tc2Config {
   static constexpr int BM = 256;                             // pair tile rows
   static constexpr int BM_CTA = 128;
-  static constexpr int BN = 256;                             // pair tile columns (UMMA N)
-  static constexpr int BN_CTA = 128;                         // B columns loaded by each CTA
+  static constexpr int BN = kBN;                             // pair tile columns (UMMA N)
+  static constexpr int BN_CTA = kBN / 2;                     // B columns each CTA supplies to the MMA
   static constexpr int STAGES = kStages;
   static constexpr int ELEM = (kDtype == 0) ? 2 : 1;
   static constexpr int KATOMS = kKAtoms;                     // 128-byte k-atoms per stage
@@ -42,7 +44,7 @@ struct Tc2Config {
   static constexpr int A_ATOM_BYTES = BM_CTA * 128;
   static constexpr int A_BYTES = KATOMS * A_ATOM_BYTES;
   static constexpr int B_CHUNK_N = 128 / ELEM;
-  static constexpr int B_CHUNKS = BN_CTA / B_CHUNK_N;
+  static constexpr int B_CHUNKS = (BN_CTA + B_CHUNK_N - 1) / B_CHUNK_N;  // boxes loaded (the last may overhang)
   static constexpr int B_CHUNK_BYTES = BK * 128;
   static constexpr int B_BYTES = B_CHUNKS * B_CHUNK_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // per CTA
@@ -51,13 +53,15 @@ struct Tc2Config {
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1 + 1;
-  static constexpr int TMEM_COLS = 512;                      // 2 accumulators x 256 columns
+  static constexpr int TMEM_COLS = 512;                      // 2 accumulators, 256 columns apart
+  static constexpr int ACC_STRIDE = 256;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 192;
   static constexpr int PARTIAL_FLOATS = BM_CTA * BN;         // one CTA's share of a tile, fp32
   static constexpr uint32_t IDESC =
-      instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ 256);
+      instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ BN);
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
+  static_assert(BN == 256 || BN == 224, "pair tiles are 256 or 224 columns wide");
 };
 
 enum : int { kUnitWhole = 0, kUnitHead = 1, kUnitPartial = 2 };
@@ -115,7 +119,8 @@ __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
 template <class Cfg>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     gemm_bias_gelu_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC_tail,
+                       const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -143,6 +148,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
+    if (Cfg::BN % 64 != 0) tma_prefetch_desc(&tmC_tail);
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&full[s], 1);                   // the leader's producer arrives (with both CTAs' bytes)
       mbar_init(&empty[s], 1);                  // one multicast commit
@@ -233,7 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::ACC_STRIDE);
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
@@ -297,7 +303,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       }
       tc_fence_after();
       const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::ACC_STRIDE);
       const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[acc]), 0);
       if (un.kind == kUnitPartial) {
         // Write this worker's fp32 partial (its k-range of the tile) and raise its flag.
@@ -368,7 +375,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           }
         };
         epilogue_rows<Cfg::BN>(
-            t_row, m0, nb * Cfg::BN, p, &tmC, ebuf, buf, lane,
+            t_row, m0, nb * Cfg::BN, p, &tmC, &tmC_tail, ebuf, buf, lane,
             [&] {
               if (lane == 0) mbar_arrive_cluster(tempty_leader);
             },

@@ -53,7 +53,8 @@ struct Variant {
   int cta_per_tile = 1;         // 2 = CTA-pair (cluster) kernel
   bool stream_k = false;        // the kernel can run a stream-K tail
   int b_chunk_n = 0;
-  void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
+  // (grid, stream, A map, B map, C map, C tail map -- used by tiles whose width is not a multiple of 64)
+  void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                     const TcParams &) = nullptr;
   // image path (pf_prepare_image): a loaded kernel with the reference ABI
   CUfunction img_fn = nullptr;
@@ -66,6 +67,7 @@ struct Variant {
 
 template <int DT, int BN, int ST, int KA>
 void launch_tc_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                    const CUtensorMap &,
                     const TcParams &p) {
   using Cfg = TcConfig<DT, BN, ST, KA>;
   pf::gemm_bias_gelu_tc<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
@@ -93,16 +95,16 @@ Variant make_tc_variant() {
   return v;
 }
 
-template <int DT, int ST, int KA>
+template <int DT, int ST, int KA, int BN>
 void launch_tc2_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
-                     const TcParams &p) {
-  using Cfg = pf::Tc2Config<DT, ST, KA>;
-  pf::gemm_bias_gelu_tc2<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+                     const CUtensorMap &ct, const TcParams &p) {
+  using Cfg = pf::Tc2Config<DT, ST, KA, BN>;
+  pf::gemm_bias_gelu_tc2<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, ct, p);
 }
 
-template <int DT, int ST, int KA = 1>
+template <int DT, int ST, int KA = 1, int BN = 256>
 Variant make_tc2_variant() {
-  using Cfg = pf::Tc2Config<DT, ST, KA>;
+  using Cfg = pf::Tc2Config<DT, ST, KA, BN>;
   Variant v;
   v.path = Path::kTensor;
   v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc2<Cfg>);
@@ -119,12 +121,13 @@ Variant make_tc2_variant() {
   v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 2;
   v.stream_k = true;
-  v.launch_tc = &launch_tc2_impl<DT, ST, KA>;
+  v.launch_tc = &launch_tc2_impl<DT, ST, KA, BN>;
   return v;
 }
 
 template <int RAW, int SPLIT>
 void launch_tf32x3_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                        const CUtensorMap &,
                         const TcParams &p) {
   using Cfg = pf::Tf32x3Config<RAW, SPLIT>;
   pf::gemm_bias_gelu_tf32x3<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
@@ -220,6 +223,7 @@ bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant
       {PF_E4M3, 128, 128, 6, 1, &make_tc_variant<1, 128, 6>},     {PF_E4M3, 256, 256, 2, 1, &make_tc2_variant<1, 2>},
       {PF_E4M3, 256, 256, 4, 1, &make_tc2_variant<1, 4>},         {PF_E4M3, 256, 256, 6, 1, &make_tc2_variant<1, 6>},
       {PF_E4M3, 256, 256, 3, 2, &make_tc2_variant<1, 3, 2>},
+      {PF_BF16, 256, 224, 3, 2, &make_tc2_variant<0, 3, 2, 224>}, {PF_E4M3, 256, 224, 3, 2, &make_tc2_variant<1, 3, 2, 224>},
       {PF_F32_3XTF32, 256, 256, 2, 1, &make_tf32x3_variant<1, 1>},
       {PF_F32_3XTF32, 256, 256, 3, 1, &make_tf32x3_variant<1, 2>},
       {PF_F32_3XTF32, 256, 256, 4, 1, &make_tf32x3_variant<2, 2>},
@@ -310,7 +314,7 @@ struct pf_ctx {
   const float *bias = nullptr;
   void *C = nullptr;
   float sa = 1.f, sb = 1.f;
-  CUtensorMap tmA{}, tmB{}, tmC{};
+  CUtensorMap tmA{}, tmB{}, tmC{}, tmCt{};  // tmCt: 32-column C boxes for the last columns of 224-wide tiles
   bool simt_vec = false;
   CUmodule module = nullptr;  // image loaded by pf_prepare_image
 
@@ -401,6 +405,17 @@ int encode_c_map(pf_ctx *c, CUtensorMap *map, void *C, int rows) {
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// The C map for a tile's last 32 columns when its width is not a multiple of 64 (bf16 C: 64-byte rows,
+// 64-byte swizzle); otherwise a copy of the main C map (never used).
+int encode_c_tail_map(pf_ctx *c, CUtensorMap *map, const CUtensorMap &main, void *C, int rows) {
+  if (c->var.bn % 64 == 0) {
+    *map = main;
+    return PF_OK;
+  }
+  return encode_2d(c, map, out_map_type(c->dtype), C, c->N, rows, c->N * pf_out_bytes(c->dtype), 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 int encode_maps(pf_ctx *c) {
   const Variant &v = c->var;
   const CUtensorMapDataType in_t = in_map_type(c->dtype);
@@ -413,7 +428,8 @@ int encode_maps(pf_ctx *c) {
   rc = encode_2d(c, &c->tmB, in_t, c->B, c->N, c->K, c->N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   // C: [M x N]; box = 128 B of columns x 32 rows.
-  return encode_c_map(c, &c->tmC, c->C, c->M);
+  if ((rc = encode_c_map(c, &c->tmC, c->C, c->M))) return rc;
+  return encode_c_tail_map(c, &c->tmCt, c->tmC, c->C, c->M);
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -498,7 +514,7 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
       p.sk_flags = c->sk_flags;
     }
     dim3 grid(workers * v.cta_per_tile);
-    v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, p);
+    v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, c->tmCt, p);
   } else if (v.path == Path::kImage) {
     // The reference's parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} (cuda_runner.cpp:182).
     const void *a = c->A, *b = c->B, *bias = c->bias;
@@ -904,11 +920,11 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
   const void *A = static_cast<const char *>(c->A) + static_cast<size_t>(r0) * c->K * e;
   void *C = static_cast<char *>(c->C) + static_cast<size_t>(r0) * c->N * o;
   if (v.path == Path::kTensor) {
-    CUtensorMap tmA, tmC;
+    CUtensorMap tmA, tmC, tmCt;
     int rc;
     if ((rc = encode_2d(c, &tmA, in_map_type(c->dtype), A, c->K, rows, c->K * e, v.a_box_k, v.a_box_rows,
                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (rc = encode_c_map(c, &tmC, C, rows)))
+        (rc = encode_c_map(c, &tmC, C, rows)) || (rc = encode_c_tail_map(c, &tmCt, tmC, C, rows)))
       return rc;
     TcParams p;
     p.bias = c->bias;
@@ -923,7 +939,7 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
-    v.launch_tc(dim3(std::min(p.num_tiles, c->max_units) * v.cta_per_tile), s, tmA, c->tmB, tmC, p);
+    v.launch_tc(dim3(std::min(p.num_tiles, c->max_units) * v.cta_per_tile), s, tmA, c->tmB, tmC, tmCt, p);
   } else if (v.path == Path::kSimt) {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (rows + v.sbm - 1) / v.sbm);
     v.launch_simt(grid, s, static_cast<const float *>(A), static_cast<const float *>(c->B), c->bias,
@@ -1179,10 +1195,14 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
 
   const CUtensorMapDataType in_t =
       dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUtensorMap tmA, tmB, tmC;
+  CUtensorMap tmA, tmB, tmC, tmCt;
   if (encode_2d(nullptr, &tmA, in_t, A, K, M, K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
       encode_2d(nullptr, &tmB, in_t, B, N, K, N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B) ||
       encode_2d(nullptr, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");
+  tmCt = tmC;
+  if (v.bn % 64 != 0 &&
+      encode_2d(nullptr, &tmCt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");
 
   TcParams p;
@@ -1202,7 +1222,7 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ce = cudaMemsetAsync(d.scratch, 0, sizeof(unsigned), s);  // the last call's status must not leak in
   if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
-  v.launch_tc(dim3(std::min(p.num_tiles, units) * v.cta_per_tile), s, tmA, tmB, tmC, p);
+  v.launch_tc(dim3(std::min(p.num_tiles, units) * v.cta_per_tile), s, tmA, tmB, tmC, tmCt, p);
   ce = cudaGetLastError();
   if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "launch: %s", cudaGetErrorString(ce));
   if (status_out) {

@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import Context, DEFAULT_TILES, ELEM_BYTES, OUT_BYTES
+from . import Context, DEFAULT_TILES, ELEM_BYTES, OUT_BYTES, default_tile
 from .dist import Ranks, shard_span
 
 
@@ -31,8 +31,8 @@ class ShardedHostGemm:
         self.dtype = dtype
         self.M, self.N, self.K = M, N, K
         self.scale_a, self.scale_b = scale_a, scale_b
-        tile = tuple(tile) if tile else DEFAULT_TILES[dtype]
-        self.r0, self.rows = shard_span(M, ranks.world, ranks.rank, tile[0])
+        self.r0, self.rows = shard_span(M, ranks.world, ranks.rank, tuple(tile or DEFAULT_TILES[dtype])[0])
+        tile = tuple(tile) if tile else default_tile(dtype, self.rows, N)
         e, o = ELEM_BYTES[dtype], OUT_BYTES[dtype]
         self.kslice = -(-K // ranks.world)                      # rows of B each rank brings in
         dev = torch.device("cuda", ranks.local_rank)

@@ -102,7 +102,8 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     if (t->BM != 128 && t->BM != 256) return set_err(c, PF_ETILE, "tensor path: BM must be 128 or 256, got %d", t->BM);
     if (t->BK != 32) return set_err(c, PF_ETILE, "tensor path: BK must be 32 words, got %d", t->BK);
     if (t->PAD != 0 && t->PAD != 1) return set_err(c, PF_ETILE, "tensor path: PAD must be 0 or 1, got %d", t->PAD);
-    if (!(t->BN == 256 || t->BN == 128 || (t->BN == 64 && dt == PF_BF16)) || (t->BM == 256 && t->BN != 256))
+    if (!(t->BN == 256 || t->BN == 128 || (t->BN == 64 && dt == PF_BF16) || (t->BN == 224 && t->BM == 256)) ||
+        (t->BM == 256 && t->BN != 256 && t->BN != 224))
       return set_err(c, PF_ETILE, "tensor path: no kernel with BM=%d BN=%d", t->BM, t->BN);
     if (t->TM < 2) return set_err(c, PF_ETILE, "tensor path: no kernel with %d stages", t->TM);
     const int e = (int)pf_elem_bytes(dt);

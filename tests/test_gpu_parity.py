@@ -141,10 +141,11 @@ def test_fp32_cfg2_gate_and_torch(ctx, oracle_mod):
 BF16_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
               (128, 128, 32, 8, 8, 0), (128, 64, 32, 8, 16, 0), (128, 64, 32, 4, 2, 0),
               (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0), (256, 256, 32, 2, 8, 0),
-              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1), (128, 128, 32, 8, 8, 1)]
+              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1), (128, 128, 32, 8, 8, 1), (256, 224, 32, 8, 8, 1),
+              (256, 224, 32, 3, 2, 1)]
 E4M3_TILES = [(128, 256, 32, 4, 16, 0), (128, 256, 32, 2, 16, 0), (128, 128, 32, 4, 16, 0),
               (128, 128, 32, 8, 4, 0), (256, 256, 32, 8, 16, 0), (256, 256, 32, 4, 4, 0),
-              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1)]
+              (256, 256, 32, 8, 8, 1), (128, 256, 32, 2, 16, 1), (256, 224, 32, 8, 8, 1)]
 
 
 @pytest.mark.parametrize("tile", BF16_TILES)
@@ -322,29 +323,32 @@ def test_pipelined_host_path_equals_device_path(ctx, name, shape, tile):
 # ---------------------------------------------------------------------------------------------
 # stream-K tail of the CTA-pair kernel
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (512, 2048, 4096)),    # 16 tiles < 74 pairs
-                                        ("cfg3_bf16_8192", (1024, 8192, 2048)),   # 128 tiles: 1.73 waves
-                                        ("cfg3_bf16_8192", (600, 1000, 1000)),    # ragged edges, K tail
-                                        ("cfg5_e4m3_16384", (1024, 4096, 2048))])
-def test_stream_k_tail_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape):
+@pytest.mark.parametrize("name,shape,bn", [("cfg3_bf16_8192", (512, 2048, 4096), 256),    # 16 tiles < 74 pairs
+                                           ("cfg3_bf16_8192", (1024, 8192, 2048), 256),   # 128 tiles: 1.73 waves
+                                           ("cfg3_bf16_8192", (600, 1000, 1000), 256),    # ragged edges, K tail
+                                           ("cfg5_e4m3_16384", (1024, 4096, 2048), 256),
+                                           ("cfg3_bf16_8192", (600, 1000, 1000), 224),    # 224-wide tiles, tail box
+                                           ("cfg5_e4m3_16384", (512, 2000, 2048), 224)])
+def test_stream_k_tail_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape, bn):
     w = wl.scaled(wl.CONFIGS[name], *shape)
     inp = wl.make_inputs(w, seed=31)
     ops = device_operands(w, inp)
     A, B, bias, C = ops
+    tile = (256, bn, 32, 8, 8, 1)
     ctx.set_stream_k(1)
     try:
-        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), ops)
+        run_pf(ctx, w, inp, tile, ops)
         a = ctx.attrs()
         assert a["grid"] == 148  # the tail spreads over every resident pair
         ref = oracle_mod.full_f64(inp.A, inp.B, inp.bias, inp.scale_a * inp.scale_b)
         err = oracle_mod.max_rel_err(ref, to_np(C))
         assert err <= TOL[w.dtype], f"stream-K: {err:.3e}"
         C2 = torch.full_like(C, float("nan"))
-        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), (A, B, bias, C2))
+        run_pf(ctx, w, inp, tile, (A, B, bias, C2))
         assert torch.equal(C, C2)  # deterministic for a given shape
         ctx.set_stream_k(0)
         C3 = torch.full_like(C, float("nan"))
-        run_pf(ctx, w, inp, (256, 256, 32, 8, 8, 1), (A, B, bias, C3))
+        run_pf(ctx, w, inp, tile, (A, B, bias, C3))
         assert max_rel_err_t(C3.float(), C.float()) <= TOL[w.dtype]
     finally:
         ctx.set_stream_k(-1)
@@ -362,3 +366,18 @@ def test_stream_k_forced_at_full_size(ctx, oracle_mod):
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
     assert err <= 2e-2
     assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= 2e-2
+
+
+@pytest.mark.parametrize("name,rows", [("cfg3_bf16_8192", 1024), ("cfg3_bf16_8192", 2048), ("cfg4_bf16_mlp", 2048)])
+def test_224_wide_tiles_for_row_shards(ctx, oracle_mod, pf, name, rows):
+    # the shards of the 4- and 8-GPU runs get 224-wide pair tiles (whole waves); full-K parity on a row sample
+    w = wl.CONFIGS[name]
+    assert pf.default_tile(w.dtype, rows, w.N)[1] == 224
+    ws = wl.scaled(w, rows, w.N, w.K)
+    inp = wl.make_inputs(ws, seed=41)
+    A, B, bias, C = device_operands(ws, inp)
+    run_pf(ctx, ws, inp, pf.default_tile(w.dtype, rows, w.N), (A, B, bias, C))
+    assert ctx.attrs()["grid"] == 2 * min(74, -(-rows // 256) * -(-w.N // 224))
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= TOL[ws.dtype]
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[ws.dtype]
