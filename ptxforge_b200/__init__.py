@@ -68,20 +68,21 @@ DEFAULT_TILES = {
 def default_tile(dtype: str, rows: int, N: int, pairs: int = 74) -> tuple:
     """The best-measured tile for a rows x N output on one GPU.
 
-    bf16 / e4m3 use CTA-pair tiles 256 rows high, 256 or 224 columns wide: the time of a launch is about the
-    number of waves of tiles over the resident pairs times the tile width, and 224-wide tiles fill whole waves
-    where 256-wide ones leave a partial last wave (8192 columns on 1024- or 2048-row shards: 37 x 224 columns
-    make 148 / 296 tiles = 2 / 4 full waves of 74 pairs).  Ties keep 256.
+    bf16 / e4m3 use CTA-pair tiles 256 rows high and, as a rule, 256 columns wide.  A 224-wide pair tile
+    measured about as slow per tile as a 256-wide one (its B rows start 224 / 112 bytes into a 128-byte line),
+    so it only pays where the 256-wide schedule's last wave of tiles is nearly empty and 224-wide tiles add no
+    wave: MLP shards of 2048 x 14336 (448 tiles, 4 in the last wave of 74 pairs) ran 6 % faster with 224;
+    8192-column shards of 1024 / 2048 rows and MLP shards of 4096 rows ran 1.6-3.7 % slower.
     """
     base = DEFAULT_TILES[dtype]
     if dtype not in ("bf16", "e4m3") or base[0] != 256:
         return base
-
-    def cost(bn):
-        tiles = -(-rows // 256) * -(-N // bn)
-        return -(-tiles // pairs) * bn
-
-    return base[:1] + (224,) + base[2:] if cost(224) < cost(256) else base
+    t256 = -(-rows // 256) * -(-N // 256)
+    t224 = -(-rows // 256) * -(-N // 224)
+    tail = t256 % pairs
+    if 0 < tail <= pairs // 10 and -(-t224 // pairs) <= -(-t256 // pairs):
+        return base[:1] + (224,) + base[2:]
+    return base
 
 
 class PFError(RuntimeError):

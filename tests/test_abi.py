@@ -71,3 +71,12 @@ def test_shard_rows_rejects_bad_arguments(pf):
         pf.shard_rows(100, 2, 2)
     with pytest.raises(pf.PFError):
         pf.shard_rows(0, 1, 0)
+
+
+def test_default_tile_choice_follows_the_measurements():
+    """224-wide pair tiles only where the 256-wide schedule leaves a nearly empty last wave (measured on B200)."""
+    import ptxforge_b200 as pf
+    assert pf.default_tile("bf16", 2048, 14336)[1] == 224      # MLP shard at 8 GPUs: 448 tiles, 4 in the last wave
+    for rows, N in [(1024, 8192), (2048, 8192), (4096, 14336), (8192, 8192), (16384, 14336)]:
+        assert pf.default_tile("bf16", rows, N) == pf.DEFAULT_TILES["bf16"], (rows, N)
+    assert pf.default_tile("f32", 2048, 2048) == pf.DEFAULT_TILES["f32"]
