@@ -101,6 +101,15 @@ __device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, 
   return false;
 }
 
+// The k-block a worker visits at step i of its unit u.  Whole tiles alternate direction from one unit to the
+// next: the pairs run their u-th tiles at about the same time, so each wave's A panels (shared with the
+// previous wave inside a raster group) are then first read where the previous wave read them last, while
+// they are still in L2, instead of after a whole wave's worth of other traffic.  Stream-K pieces keep
+// ascending order (their partial sums are indexed by k range, not by order).
+__device__ __forceinline__ int unit_kb(const SkUnit &un, int u, int i) {
+  return (un.kind == kUnitWhole && (u & 1)) ? un.kb1 - 1 - i : un.kb0 + i;
+}
+
 // First k-iteration (in the tail's linear k space) owned by worker w.
 __device__ __forceinline__ long long sk_start(int w, int W, const TcParams &p) {
   return static_cast<long long>(w) * p.sk_iters / W;
@@ -191,7 +200,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         tile_coords(un.tile, p, mb, nb);
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
+          const int kb = unit_kb(un, u, i);
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
@@ -240,7 +250,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::ACC_STRIDE);
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
@@ -255,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             const uint64_t ad =
                 smem_desc(a_addr + (k / PER_ATOM) * Cfg::A_ATOM_BYTES + (k % PER_ATOM) * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
-            const uint32_t accumulate = (kb != un.kb0 || k != 0) ? 1u : 0u;
+            const uint32_t accumulate = (i != 0 || k != 0) ? 1u : 0u;
             if constexpr (Cfg::ELEM == 2)
               tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, accumulate);
             else
