@@ -2,7 +2,9 @@
 //
 // Persistent, warp-specialised kernel for sm_100a (one CTA per SM, 192 threads):
 //   warp 0      TMA producer: one elected lane streams A (K-major) and B (N-major) k-blocks into a
-//               STAGES-deep ring of 128-byte-swizzled shared-memory tiles (full/empty mbarriers).
+//               STAGES-deep ring of 128-byte-swizzled shared-memory tiles (full/empty mbarriers); every
+//               other tile of a CTA walks k downwards, so the CTAs' next wave of tiles starts on the A and
+//               B slabs the previous wave read last (still in L2).
 //   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 bf16 /
 //               32 e4m3) into a double-buffered fp32 accumulator (2 x BN TMEM columns) and
 //               tcgen05.commit's the smem stage back to the producer and the finished accumulator
@@ -272,10 +274,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x, j = 0; t < p.num_tiles && ok; t += gridDim.x, ++j) {
         int mb, nb;
         tile_coords(t, p, mb, nb);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int i = 0; i < p.k_blocks; ++i) {
+          const int kb = (j & 1) ? p.k_blocks - 1 - i : i;  // every other tile walks k downwards
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int i = 0; i < p.k_blocks; ++i) {
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
@@ -342,9 +345,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             // B: N-major, 128-B swizzle; k advances UMMA_K rows of 128 B; LBO = next 128-B column chunk.
             const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
             if constexpr (Cfg::ELEM == 2)
-              tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+              tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (i | k) != 0);
             else
-              tc_mma_f8(d_tmem, ad, bd, Cfg::IDESC, (kb | k) != 0);
+              tc_mma_f8(d_tmem, ad, bd, Cfg::IDESC, (i | k) != 0);
           }
           tc_commit(&empty[stage]);
           if (++stage == Cfg::STAGES) {
