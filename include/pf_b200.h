@@ -178,6 +178,15 @@ int pf_upload(pf_ctx *ctx, const void *hA, const void *hB, const float *hbias, f
               float scale_b);
 int pf_download(pf_ctx *ctx, void *hC);
 
+/* pf_run_host for a row shard whose B and bias are already on the device (e.g. all-gathered over
+ * NVLink): copies the host rows hA into the bound A buffer, launches, and copies C (the bound C buffer)
+ * back to hC, in up to 8 row chunks whose H2D copies, kernels and D2H copies overlap, then synchronises.
+ * Requires pf_prepare + pf_bind with caller-owned device A, B, bias and C; the bound A and C buffers are
+ * overwritten.  The work starts after everything already queued on `after_stream` (a cudaStream_t, NULL =
+ * the CUDA default stream), where the caller produced B and bias.  The row-shard counterpart of
+ * pf_run_host (same reference call sites, cuda_runner.cpp:91-108, 183-188). */
+int pf_run_host_rows(pf_ctx *ctx, const void *hA, void *hC, void *after_stream);
+
 /* ---- row sharding (no collective on the hot path) ----------------------------------------- */
 
 /* Rows [*row0, *row0 + *rows) of A and C that shard `g` of `G` owns for an M-row problem.  Shard

@@ -31,7 +31,7 @@ SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
            "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
            "pf_gemm_bias_gelu_noalloc", "pf_prepare_image", "pf_time_cublas",
-           "pf_set_stream_k")
+           "pf_set_stream_k", "pf_run_host_rows")
 
 
 class Tile(ctypes.Structure):
@@ -120,6 +120,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_last_error.argtypes = [vp]
         lib.pf_last_error.restype = ctypes.c_char_p
         lib.pf_run_host.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
+        lib.pf_run_host_rows.argtypes = [vp, vp, vp, vp]
         lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
         lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_download.argtypes = [vp, vp]
@@ -137,7 +138,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_version.restype = ctypes.c_char_p
         lib.pf_selftest_wait_timeout.argtypes = [vp, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
-                     "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_shard_rows",
+                     "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_run_host_rows", "pf_shard_rows",
                      "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc",
                      "pf_prepare_image", "pf_time_cublas", "pf_set_stream_k"):
             getattr(lib, name).restype = ctypes.c_int
@@ -169,6 +170,11 @@ def _ptr(x) -> int:
     if hasattr(x, "ctypes"):
         return int(x.ctypes.data)
     raise TypeError(f"cannot take a device/host pointer of {type(x)}")
+
+
+def _stream(s) -> int:
+    """A cudaStream_t handle from None (the CUDA default stream), an int or a torch stream."""
+    return 0 if s is None else (s if isinstance(s, int) else int(s.cuda_stream))
 
 
 class Context:
@@ -227,8 +233,7 @@ class Context:
         return self
 
     def launch(self, stream=None):
-        s = 0 if stream is None else (stream if isinstance(stream, int) else int(stream.cuda_stream))
-        self._check(self._lib.pf_launch(self._h, s), "pf_launch")
+        self._check(self._lib.pf_launch(self._h, _stream(stream)), "pf_launch")
 
     def time(self, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
         ms = ctypes.c_double()
@@ -264,6 +269,12 @@ class Context:
         """H2D copies of host operands, launch, D2H of C, synchronise (pf_run_host)."""
         self._check(self._lib.pf_run_host(self._h, _ptr(hA), _ptr(hB), _ptr(hbias), _ptr(hC), scale_a, scale_b),
                     "pf_run_host")
+
+    def run_host_rows(self, hA, hC, after_stream=None):
+        """Host rows of A in, launch, C rows out, pipelined in row chunks, with B and bias already on the
+        device (bound) -- after everything queued on `after_stream` (pf_run_host_rows)."""
+        self._check(self._lib.pf_run_host_rows(self._h, _ptr(hA), _ptr(hC), _stream(after_stream)),
+                    "pf_run_host_rows")
 
     def upload(self, hA, hB, hbias, scale_a: float = 1.0, scale_b: float = 1.0):
         """H2D copies into context-owned device operands and bind them (pf_upload)."""

@@ -1016,6 +1016,52 @@ int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, v
   return PF_OK;
 }
 
+int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream) {
+  if (!c) return PF_EINVAL;
+  if (!c->prepared || !c->bound) return set_err(c, PF_ESTATE, "pf_run_host_rows before pf_prepare / pf_bind");
+  if (!hA || !hC) return set_err(c, PF_EINVAL, "null host operand");
+  if (c->var.path == Path::kImage) return set_err(c, PF_ESTATE, "pf_run_host_rows on a loaded image");
+  DeviceGuard g(c->device);
+  const size_t e = pf_elem_bytes(c->dtype), o = pf_out_bytes(c->dtype);
+  const size_t rowA = static_cast<size_t>(c->K) * e, rowC = static_cast<size_t>(c->N) * o;
+  const int align = c->var.path == Path::kTensor ? c->var.bm : c->var.sbm;
+  const int units = (c->M + align - 1) / align;
+  const int P = std::max(1, std::min(8, units));
+  if (!c->s_comp) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_comp, cudaStreamNonBlocking));
+  if (!c->s_out) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
+  while (c->ev_pool.size() < static_cast<size_t>(2 * P + 1)) {
+    cudaEvent_t ev;
+    PF_CUDA(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    c->ev_pool.push_back(ev);
+  }
+  // B and bias are produced on the caller's stream (an upload, an all-gather): the kernels wait for it.
+  cudaEvent_t evB = c->ev_pool[0];
+  PF_CUDA(c, cudaEventRecord(evB, static_cast<cudaStream_t>(after_stream)));
+  PF_CUDA(c, cudaStreamWaitEvent(c->s_comp, evB, 0));
+  PF_CUDA(c, cudaStreamWaitEvent(c->stream, evB, 0));  // the bound A may still be read by an earlier launch
+  for (int i = 0; i < P; ++i) {
+    const int r0 = static_cast<int>(static_cast<long long>(units) * i / P) * align;
+    const int r1 = std::min(c->M, static_cast<int>(static_cast<long long>(units) * (i + 1) / P) * align);
+    if (r1 <= r0) continue;
+    cudaEvent_t evA = c->ev_pool[1 + 2 * i], evC = c->ev_pool[2 + 2 * i];
+    PF_CUDA(c, cudaMemcpyAsync(static_cast<char *>(const_cast<void *>(c->A)) + r0 * rowA,
+                               static_cast<const char *>(hA) + r0 * rowA, (r1 - r0) * rowA, cudaMemcpyHostToDevice,
+                               c->stream));
+    PF_CUDA(c, cudaEventRecord(evA, c->stream));
+    PF_CUDA(c, cudaStreamWaitEvent(c->s_comp, evA, 0));
+    int rc;
+    if ((rc = P == 1 ? do_launch(c, c->s_comp) : launch_rows(c, c->s_comp, r0, r1 - r0))) return rc;
+    PF_CUDA(c, cudaEventRecord(evC, c->s_comp));
+    PF_CUDA(c, cudaStreamWaitEvent(c->s_out, evC, 0));
+    PF_CUDA(c, cudaMemcpyAsync(static_cast<char *>(hC) + r0 * rowC, static_cast<char *>(c->C) + r0 * rowC,
+                               (r1 - r0) * rowC, cudaMemcpyDeviceToHost, c->s_out));
+  }
+  PF_CUDA(c, cudaStreamSynchronize(c->s_out));
+  PF_CUDA(c, cudaStreamSynchronize(c->s_comp));
+  PF_CUDA(c, cudaStreamSynchronize(c->stream));
+  return PF_OK;
+}
+
 int pf_upload(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
   if (!c) return PF_EINVAL;
   if (!c->prepared) return set_err(c, PF_ESTATE, "pf_upload before pf_prepare");

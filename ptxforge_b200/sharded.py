@@ -4,8 +4,8 @@ Every rank owns rows `shard_span(M, world, rank)` of A and C; B and bias are nee
 Instead of every rank copying all of B from host memory over its PCIe link, rank r copies only rows
 [r*Kp/world, (r+1)*Kp/world) of B (Kp = K rounded up to a multiple of world) and the slices are
 all-gathered over NVLink (NCCL, in place), so each input byte crosses PCIe once per step in total.
-Then the kernel runs on the local rows (no collective on the compute path) and the rank's rows of C go
-back to host memory.  RowGather is the optional, separately timed all-gather of C's row shards for
+Then the rank's rows of A go in, the kernel runs on them and its rows of C come back in overlapping row
+chunks (pf_run_host_rows: H2D of A, kernels and D2H of C pipelined; no collective on the compute path).  RowGather is the optional, separately timed all-gather of C's row shards for
 consumers that need the whole result on every GPU.
 
     ranks = Ranks("nccl")
@@ -56,7 +56,8 @@ class ShardedHostGemm:
         return x.reshape(-1).view(torch.uint8)
 
     def __call__(self, hA_rows, hB, hbias, hC_rows):
-        """One step: H2D of this rank's A rows and B slice, NCCL all-gather of B, kernel, D2H of C rows."""
+        """One step: H2D of this rank's B slice, NCCL all-gather of B, then its A rows in / kernel / C rows
+        out, pipelined in row chunks."""
         torch = self.torch
         dist = self.ranks.pg
         stream = torch.cuda.current_stream()
@@ -69,14 +70,11 @@ class ShardedHostGemm:
         mine = self.Bp[rank * slice_bytes:(rank + 1) * slice_bytes]
         if k1 > k0:
             mine[:(k1 - k0) * N * e].copy_(hb[k0 * N * e:k1 * N * e], non_blocking=True)
-        if self.rows:
-            self.A.copy_(self._bytes(hA_rows), non_blocking=True)
         self.bias.copy_(self._bytes(hbias).view(torch.float32), non_blocking=True)
         if dist is not None and world > 1:
             dist.all_gather_into_tensor(self.Bp, mine)
         if self.rows:
-            self.ctx.launch(stream)
-            self._bytes(hC_rows).copy_(self.C[:self.rows * N * self.o], non_blocking=True)
+            self.ctx.run_host_rows(self._bytes(hA_rows), self._bytes(hC_rows), after_stream=stream)
         stream.synchronize()
 
     def h2d_bytes(self) -> int:

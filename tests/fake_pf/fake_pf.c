@@ -255,6 +255,19 @@ static int ensure(void **buf, size_t n) {
   return *buf ? PF_OK : PF_ENOMEM;
 }
 
+int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream) {
+  (void)after_stream;
+  if (!c) return PF_EINVAL;
+  if (!c->prepared || !c->bound) return set_err(c, PF_ESTATE, "pf_run_host_rows before pf_prepare / pf_bind");
+  if (!hA || !hC) return set_err(c, PF_EINVAL, "null host operand");
+  /* "device" memory is host memory here: rows of A into the bound A, launch, C back */
+  memcpy((void *)c->A, hA, (size_t)c->M * c->K * pf_elem_bytes(c->dtype));
+  int rc = pf_launch(c, NULL);
+  if (rc) return rc;
+  memcpy(hC, c->C, (size_t)c->M * c->N * pf_out_bytes(c->dtype));
+  return PF_OK;
+}
+
 int pf_upload(pf_ctx *c, const void *hA, const void *hB, const float *hbias, float sa, float sb) {
   if (!c) return PF_EINVAL;
   if (!c->prepared) return set_err(c, PF_ESTATE, "pf_upload before pf_prepare");

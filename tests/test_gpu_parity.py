@@ -381,3 +381,27 @@ def test_224_wide_tiles_on_row_shards(ctx, oracle_mod, pf, name, rows):
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
     assert err <= TOL[ws.dtype]
     assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[ws.dtype]
+
+
+@pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (2048, 1024, 768)), ("cfg5_e4m3_16384", (1000, 512, 512)),
+                                        ("cfg2_f32_2048", (1030, 256, 128))])
+def test_run_host_rows_equals_device_path(ctx, name, shape):
+    # pf_run_host_rows: B and bias already on the device (bound); host rows of A in, C rows out, in chunks
+    w = wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w, seed=23)
+    A, B, bias, C = device_operands(w, inp)
+    ctx.set_stream_k(0)
+    try:
+        run_pf(ctx, w, inp, None, (A, B, bias, C))
+        A2, C2 = torch.zeros_like(A), torch.full_like(C, float("nan"))
+        ctx.prepare(w.dtype, None, w.M, w.N, w.K)
+        ctx.bind(A2, B, bias, C2, inp.scale_a, inp.scale_b)
+        hA = torch.from_numpy(np.ascontiguousarray(inp.A_raw)).pin_memory()
+        hC = torch.empty(C.numel() * C.element_size(), dtype=torch.uint8).pin_memory()
+        ctx.run_host_rows(hA, hC, after_stream=torch.cuda.current_stream())
+        assert ctx.status() == 0
+    finally:
+        ctx.set_stream_k(-1)
+    want = C.reshape(-1).view(torch.uint8).cpu()
+    assert torch.equal(hC, want)
+    assert torch.equal(A2.reshape(-1).view(torch.uint8).cpu(), hA.reshape(-1).view(torch.uint8))
