@@ -5,8 +5,9 @@ Instead of every rank copying all of B from host memory over its PCIe link, rank
 [r*Kp/world, (r+1)*Kp/world) of B (Kp = K rounded up to a multiple of world) and the slices are
 all-gathered over NVLink (NCCL, in place), so each input byte crosses PCIe once per step in total.
 Then the rank's rows of A go in, the kernel runs on them and its rows of C come back in overlapping row
-chunks (pf_run_host_rows: H2D of A, kernels and D2H of C pipelined; no collective on the compute path).  RowGather is the optional, separately timed all-gather of C's row shards for
-consumers that need the whole result on every GPU.
+chunks (pf_run_host_rows: H2D of A, kernels and D2H of C pipelined; no collective on the compute path).
+RowGather is the optional, separately timed all-gather of C's row shards for consumers that need the whole
+result on every GPU.
 
     ranks = Ranks("nccl")
     run = ShardedHostGemm(ranks, "bf16", None, M, N, K)
