@@ -3,8 +3,8 @@
 // Persistent, warp-specialised kernel for sm_100a (one CTA per SM, 192 threads):
 //   warp 0      TMA producer: one elected lane streams A (K-major) and B (N-major) k-blocks into a
 //               STAGES-deep ring of 128-byte-swizzled shared-memory tiles (full/empty mbarriers); every
-//               other tile of a CTA walks k downwards, so the CTAs' next wave of tiles starts on the A and
-//               B slabs the previous wave read last (still in L2).
+//               other wave of tiles walks k downwards (tile_k_reversed), so the next wave starts on the A
+//               and B slabs the previous wave read last (still in L2).
 //   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma (M=128, N=BN, K=16 bf16 /
 //               32 e4m3) into a double-buffered fp32 accumulator (2 x BN TMEM columns) and
 //               tcgen05.commit's the smem stage back to the producer and the finished accumulator
@@ -47,6 +47,13 @@ struct TcParams {
   unsigned epoch = 0;      // this launch's tag for the partial-ready flags
   float *sk_partials = nullptr;    // [workers][2 CTAs][128 x 256] fp32
   unsigned *sk_flags = nullptr;    // [workers][2 CTAs]
+  // The schedule that sets each tile's k direction (tile_k_reversed): 0 = this launch's own.  A launch over a
+  // window of rows of a larger bound problem passes the whole problem's, so its tiles are summed in the same
+  // order -- and give the same bits -- as in one launch over the whole problem.
+  int dir_m0 = 0;             // first row block of this launch within the whole problem
+  int dir_num_m_blocks = 0;   // row blocks of the whole problem
+  int dir_group_m = 0;        // raster group of the whole problem's launch
+  int dir_workers = 0;        // workers (CTAs or CTA pairs) of the whole problem's launch
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).
@@ -95,6 +102,20 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams &p, int &mb, i
   const int r = t - g * per_group;
   mb = first_m + r % rows;
   nb = r / rows;
+}
+
+// Whether tile (mb, nb) walks k downwards: every other wave of the whole problem's schedule does (tile t of
+// the raster order is a worker's (t / workers)-th tile), so each wave starts on the k slabs of its raster
+// group's A (and B) panels that the previous wave read last, while they are still in L2.
+__device__ __forceinline__ bool tile_k_reversed(const TcParams &p, int mb, int nb, int launch_workers) {
+  const int num_m = p.dir_num_m_blocks ? p.dir_num_m_blocks : p.num_m_blocks;
+  const int group = p.dir_group_m ? p.dir_group_m : p.group_m;
+  const int workers = p.dir_workers ? p.dir_workers : launch_workers;
+  const int m = mb + p.dir_m0;
+  const int g = m / group, first_m = g * group;
+  const int rows = min(num_m - first_m, group);
+  const long long t = static_cast<long long>(g) * group * p.num_n_blocks + static_cast<long long>(nb) * rows + (m - first_m);
+  return ((t / workers) & 1) != 0;
 }
 
 __device__ __forceinline__ float gelu_tanh_fast(float x) {
@@ -274,11 +295,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x, j = 0; t < p.num_tiles && ok; t += gridDim.x, ++j) {
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(t, p, mb, nb);
+        const bool reversed = tile_k_reversed(p, mb, nb, gridDim.x);
         for (int i = 0; i < p.k_blocks; ++i) {
-          const int kb = (j & 1) ? p.k_blocks - 1 - i : i;  // every other tile walks k downwards
+          const int kb = reversed ? p.k_blocks - 1 - i : i;
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;

@@ -101,13 +101,13 @@ __device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, 
   return false;
 }
 
-// The k-block a worker visits at step i of its unit u.  Whole tiles alternate direction from one unit to the
-// next: the pairs run their u-th tiles at about the same time, so each wave's A panels (shared with the
-// previous wave inside a raster group) are then first read where the previous wave read them last, while
-// they are still in L2, instead of after a whole wave's worth of other traffic.  Stream-K pieces keep
+// The k-block visited at step i of a unit.  Whole tiles of every other wave walk k downwards
+// (tile_k_reversed): the pairs run a wave's tiles at about the same time, so each wave's A panels (shared
+// with the previous wave inside a raster group) are then first read where the previous wave read them last,
+// while they are still in L2, instead of after a whole wave's worth of other traffic.  Stream-K pieces keep
 // ascending order (their partial sums are indexed by k range, not by order).
-__device__ __forceinline__ int unit_kb(const SkUnit &un, int u, int i) {
-  return (un.kind == kUnitWhole && (u & 1)) ? un.kb1 - 1 - i : un.kb0 + i;
+__device__ __forceinline__ int unit_kb(const SkUnit &un, bool reversed, int i) {
+  return (un.kind == kUnitWhole && reversed) ? un.kb1 - 1 - i : un.kb0 + i;
 }
 
 // First k-iteration (in the tail's linear k space) owned by worker w.
@@ -200,8 +200,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         tile_coords(un.tile, p, mb, nb);
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
+        const bool reversed = tile_k_reversed(p, mb, nb, num_pairs);
         for (int i = 0; i < un.kb1 - un.kb0; ++i) {
-          const int kb = unit_kb(un, u, i);
+          const int kb = unit_kb(un, reversed, i);
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;

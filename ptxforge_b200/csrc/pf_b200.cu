@@ -939,6 +939,13 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
+    // k directions as in one launch over the whole bound problem (the same bits as do_launch)
+    const int full_m_blocks = (c->M + v.bm - 1) / v.bm;
+    const int full_tiles = full_m_blocks * p.num_n_blocks;
+    p.dir_m0 = r0 / v.bm;
+    p.dir_num_m_blocks = full_m_blocks;
+    p.dir_group_m = std::max(1, std::min(c->group_m, full_m_blocks));
+    p.dir_workers = sk_tail_tiles(c, full_tiles, p.k_blocks) > 0 ? c->max_units : std::min(full_tiles, c->max_units);
     v.launch_tc(dim3(std::min(p.num_tiles, c->max_units) * v.cta_per_tile), s, tmA, c->tmB, tmC, tmCt, p);
   } else if (v.path == Path::kSimt) {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (rows + v.sbm - 1) / v.sbm);

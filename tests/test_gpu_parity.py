@@ -302,6 +302,8 @@ def test_cublas_comparator(ctx, name, shape):
 
 
 @pytest.mark.parametrize("name,shape,tile", [("cfg3_bf16_8192", (2048, 1024, 768), None),
+                                             ("cfg3_bf16_8192", (4096, 4096, 512), None),   # 256 tiles: 3.5 waves
+                                             ("cfg3_bf16_8192", (4096, 4096, 512), (128, 256, 32, 4, 16, 0)),
                                              ("cfg3_bf16_8192", (1000, 520, 264), (128, 256, 32, 4, 16, 0)),
                                              ("cfg5_e4m3_16384", (1536, 512, 512), None),
                                              ("cfg2_f32_2048", (1030, 256, 128), None)])
@@ -384,6 +386,7 @@ def test_224_wide_tiles_on_row_shards(ctx, oracle_mod, pf, name, rows):
 
 
 @pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (2048, 1024, 768)), ("cfg5_e4m3_16384", (1000, 512, 512)),
+                                        ("cfg3_bf16_8192", (4096, 4096, 512)),
                                         ("cfg2_f32_2048", (1030, 256, 128))])
 def test_run_host_rows_equals_device_path(ctx, name, shape):
     # pf_run_host_rows: B and bias already on the device (bound); host rows of A in, C rows out, in chunks
