@@ -293,8 +293,8 @@ def run_ours(args, dist):
         from ptxforge_b200.sharded import ShardedHostGemm
         ctx_e2e = ShardedHostGemm(dist, w.dtype, tile, w.M, w.N, w.K, inp.scale_a, inp.scale_b)
         step = lambda: ctx_e2e(pin["A"], pin["B"], pin["bias"], hC)  # noqa: E731
-        e2e_api = ("ShardedHostGemm: pinned host buffers, per-rank H2D of its A rows and 1/N of B, "
-                   "NCCL all-gather of B over NVLink, kernel, D2H of its C rows")
+        e2e_api = ("ShardedHostGemm: pinned host buffers, per-rank H2D of 1/N of B, NCCL all-gather of B over "
+                   "NVLink, then its A rows in / kernel / C rows out in overlapping row chunks (pf_run_host_rows)")
         h2d, d2h = ctx_e2e.h2d_bytes(), ctx_e2e.d2h_bytes()
     step()  # warm: allocations, first-use set-up
     dist.barrier()
