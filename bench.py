@@ -12,8 +12,8 @@ fixed).  FLOPs are 2*M*N*K (the epilogue is not counted, as in the reference, sp
 Besides the device-timed `value`, the line carries
   e2e           the same metric end to end from pinned host buffers, every step: at N=1 the C ABI's
                 pf_run_host (H2D of A, B, bias, the kernel, D2H of C, overlapped in row chunks); at N>1
-                ptxforge_b200.sharded.ShardedHostGemm (each rank copies its A rows and 1/N of B, B is
-                all-gathered over NVLink, kernel on the local rows, D2H of its C rows)
+                ptxforge_b200.sharded.ShardedHostGemm (each rank copies 1/N of B, B is all-gathered over
+                NVLink, then its A rows in / kernel / C rows out overlap in row chunks, pf_run_host_rows)
   roofline      achieved TFLOP/s of the kernel over the measured dense bf16 peak
   comparators   cuBLAS GEMM alone and cuBLAS + a separate bias+GELU pass (pf_time_cublas), same inputs
   cpu_baseline  the CPU-lowered schedule (oracle port) on the host cores, on a bounded sample (N=1)
