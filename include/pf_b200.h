@@ -182,10 +182,13 @@ int pf_download(pf_ctx *ctx, void *hC);
  * NVLink): copies the host rows hA into the bound A buffer, launches, and copies C (the bound C buffer)
  * back to hC, in up to 8 row chunks whose H2D copies, kernels and D2H copies overlap, then synchronises.
  * Requires pf_prepare + pf_bind with caller-owned device A, B, bias and C; the bound A and C buffers are
- * overwritten.  The work starts after everything already queued on `after_stream` (a cudaStream_t, NULL =
- * the CUDA default stream), where the caller produced B and bias.  The row-shard counterpart of
- * pf_run_host (same reference call sites, cuda_runner.cpp:91-108, 183-188). */
-int pf_run_host_rows(pf_ctx *ctx, const void *hA, void *hC, void *after_stream);
+ * overwritten, so no work that reads them may still be in flight.  The kernels start after everything
+ * queued on `after_stream` (where the caller produced B and bias), the copies of A after everything queued
+ * on `copies_after_stream` (e.g. the copy of this rank's slice of B, so the host link carries B first and
+ * then A while B is all-gathered); pass the same stream twice to order everything after it (cudaStream_t
+ * handles, NULL = the CUDA default stream).  The row-shard counterpart of pf_run_host (same reference call
+ * sites, cuda_runner.cpp:91-108, 183-188); one launch over the shard gives the same bits. */
+int pf_run_host_rows(pf_ctx *ctx, const void *hA, void *hC, void *after_stream, void *copies_after_stream);
 
 /* ---- row sharding (no collective on the hot path) ----------------------------------------- */
 

@@ -120,7 +120,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.pf_last_error.argtypes = [vp]
         lib.pf_last_error.restype = ctypes.c_char_p
         lib.pf_run_host.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
-        lib.pf_run_host_rows.argtypes = [vp, vp, vp, vp]
+        lib.pf_run_host_rows.argtypes = [vp, vp, vp, vp, vp]
         lib.pf_shard_rows.argtypes = [i, i, i, i, ip, ip]
         lib.pf_upload.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float]
         lib.pf_download.argtypes = [vp, vp]
@@ -270,11 +270,13 @@ class Context:
         self._check(self._lib.pf_run_host(self._h, _ptr(hA), _ptr(hB), _ptr(hbias), _ptr(hC), scale_a, scale_b),
                     "pf_run_host")
 
-    def run_host_rows(self, hA, hC, after_stream=None):
+    def run_host_rows(self, hA, hC, after_stream=None, copies_after_stream=None):
         """Host rows of A in, launch, C rows out, pipelined in row chunks, with B and bias already on the
-        device (bound) -- after everything queued on `after_stream` (pf_run_host_rows)."""
-        self._check(self._lib.pf_run_host_rows(self._h, _ptr(hA), _ptr(hC), _stream(after_stream)),
-                    "pf_run_host_rows")
+        device (bound): kernels after the work queued on `after_stream`, copies of A after the work queued on
+        `copies_after_stream` (default: the same stream) (pf_run_host_rows)."""
+        s = _stream(after_stream)
+        cs = s if copies_after_stream is None else _stream(copies_after_stream)
+        self._check(self._lib.pf_run_host_rows(self._h, _ptr(hA), _ptr(hC), s, cs), "pf_run_host_rows")
 
     def upload(self, hA, hB, hbias, scale_a: float = 1.0, scale_b: float = 1.0):
         """H2D copies into context-owned device operands and bind them (pf_upload)."""

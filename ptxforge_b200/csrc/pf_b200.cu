@@ -1023,7 +1023,7 @@ int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, v
   return PF_OK;
 }
 
-int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream) {
+int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream, void *copies_after_stream) {
   if (!c) return PF_EINVAL;
   if (!c->prepared || !c->bound) return set_err(c, PF_ESTATE, "pf_run_host_rows before pf_prepare / pf_bind");
   if (!hA || !hC) return set_err(c, PF_EINVAL, "null host operand");
@@ -1041,11 +1041,24 @@ int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream) {
     PF_CUDA(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     c->ev_pool.push_back(ev);
   }
-  // B and bias are produced on the caller's stream (an upload, an all-gather): the kernels wait for it.
+  // B and bias are produced on `after_stream` (an upload, an all-gather): the kernels wait for it.  The
+  // copies of A wait only for `copies_after_stream` -- e.g. the copy of this rank's slice of B, so that the
+  // host link carries B first and then A while the all-gather runs over NVLink.
   cudaEvent_t evB = c->ev_pool[0];
   PF_CUDA(c, cudaEventRecord(evB, static_cast<cudaStream_t>(after_stream)));
   PF_CUDA(c, cudaStreamWaitEvent(c->s_comp, evB, 0));
-  PF_CUDA(c, cudaStreamWaitEvent(c->stream, evB, 0));  // the bound A may still be read by an earlier launch
+  if (copies_after_stream != after_stream) {
+    if (c->ev_pool.size() < static_cast<size_t>(2 * P + 2)) {
+      cudaEvent_t ev;
+      PF_CUDA(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      c->ev_pool.push_back(ev);
+    }
+    cudaEvent_t evCopy = c->ev_pool[2 * P + 1];
+    PF_CUDA(c, cudaEventRecord(evCopy, static_cast<cudaStream_t>(copies_after_stream)));
+    PF_CUDA(c, cudaStreamWaitEvent(c->stream, evCopy, 0));
+  } else {
+    PF_CUDA(c, cudaStreamWaitEvent(c->stream, evB, 0));
+  }
   for (int i = 0; i < P; ++i) {
     const int r0 = static_cast<int>(static_cast<long long>(units) * i / P) * align;
     const int r1 = std::min(c->M, static_cast<int>(static_cast<long long>(units) * (i + 1) / P) * align);

@@ -42,6 +42,7 @@ class ShardedHostGemm:
         self.Bp = torch.empty(self.kslice * ranks.world * N * e, dtype=u8, device=dev)  # padded K rows
         self.bias = torch.empty(N, dtype=torch.float32, device=dev)
         self.C = torch.empty(max(1, self.rows) * N * o, dtype=u8, device=dev)
+        self.copy_stream = torch.cuda.Stream(device=dev)          # host -> device copy of B's slice
         self.ctx = Context(ranks.local_rank)
         if self.rows:
             self.ctx.prepare(dtype, tile, self.rows, N, K)
@@ -58,7 +59,8 @@ class ShardedHostGemm:
 
     def __call__(self, hA_rows, hB, hbias, hC_rows):
         """One step: H2D of this rank's B slice, NCCL all-gather of B, then its A rows in / kernel / C rows
-        out, pipelined in row chunks."""
+        out, pipelined in row chunks.  The host link carries B's slice first and A's rows right after it,
+        while the all-gather runs over NVLink; the kernels wait for the gather."""
         torch = self.torch
         dist = self.ranks.pg
         stream = torch.cuda.current_stream()
@@ -69,13 +71,17 @@ class ShardedHostGemm:
         hb = self._bytes(hB)
         slice_bytes = self.kslice * N * e
         mine = self.Bp[rank * slice_bytes:(rank + 1) * slice_bytes]
-        if k1 > k0:
-            mine[:(k1 - k0) * N * e].copy_(hb[k0 * N * e:k1 * N * e], non_blocking=True)
-        self.bias.copy_(self._bytes(hbias).view(torch.float32), non_blocking=True)
+        self.copy_stream.wait_stream(stream)
+        with torch.cuda.stream(self.copy_stream):
+            if k1 > k0:
+                mine[:(k1 - k0) * N * e].copy_(hb[k0 * N * e:k1 * N * e], non_blocking=True)
+            self.bias.copy_(self._bytes(hbias).view(torch.float32), non_blocking=True)
+        stream.wait_stream(self.copy_stream)
         if dist is not None and world > 1:
             dist.all_gather_into_tensor(self.Bp, mine)
         if self.rows:
-            self.ctx.run_host_rows(self._bytes(hA_rows), self._bytes(hC_rows), after_stream=stream)
+            self.ctx.run_host_rows(self._bytes(hA_rows), self._bytes(hC_rows), after_stream=stream,
+                                   copies_after_stream=self.copy_stream)
         stream.synchronize()
 
     def h2d_bytes(self) -> int:

@@ -255,8 +255,9 @@ static int ensure(void **buf, size_t n) {
   return *buf ? PF_OK : PF_ENOMEM;
 }
 
-int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream) {
+int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream, void *copies_after_stream) {
   (void)after_stream;
+  (void)copies_after_stream;
   if (!c) return PF_EINVAL;
   if (!c->prepared || !c->bound) return set_err(c, PF_ESTATE, "pf_run_host_rows before pf_prepare / pf_bind");
   if (!hA || !hC) return set_err(c, PF_EINVAL, "null host operand");

@@ -401,7 +401,9 @@ def test_run_host_rows_equals_device_path(ctx, name, shape):
         ctx.bind(A2, B, bias, C2, inp.scale_a, inp.scale_b)
         hA = torch.from_numpy(np.ascontiguousarray(inp.A_raw)).pin_memory()
         hC = torch.empty(C.numel() * C.element_size(), dtype=torch.uint8).pin_memory()
-        ctx.run_host_rows(hA, hC, after_stream=torch.cuda.current_stream())
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        ctx.run_host_rows(hA, hC, after_stream=torch.cuda.current_stream(), copies_after_stream=side)
         assert ctx.status() == 0
     finally:
         ctx.set_stream_k(-1)
