@@ -68,6 +68,24 @@ def mt_stream(seed: int, n: int) -> np.ndarray:
     return out
 
 
+def uniform_f32(seed: int, n: int, a: float = -0.5, b: float = 0.5) -> np.ndarray:
+    """n draws of std::uniform_real_distribution<float>(a, b) from std::mt19937(seed), as libstdc++ makes
+    them: generate_canonical<float, 24> takes one 32-bit output w and forms u = float(w) / 2^32 in float
+    arithmetic (a quotient of 1 becomes the largest float below 1); the value is u * (b - a) + a."""
+    u = mt_stream(seed, n).astype(np.float32) / np.float32(4294967296.0)
+    u = np.where(u >= np.float32(1), np.nextafter(np.float32(1), np.float32(0)), u)
+    return (u * (np.float32(b) - np.float32(a)) + np.float32(a)).astype(np.float32)
+
+
+def runner_inputs(M: int, N: int, K: int):
+    """The reference runner's own inputs (CudaRunner::Impl::ensure, core/src/cuda_runner.cpp:97-102): one
+    std::mt19937(1234) stream through U(-0.5, 0.5), filling A (M x K), then B (K x N), then bias (N)."""
+    v = uniform_f32(1234, M * K + K * N + N)
+    A = v[:M * K].reshape(M, K)
+    B = v[M * K:M * K + K * N].reshape(K, N)
+    return A, B, v[M * K + K * N:]
+
+
 def gelu_f64(x: float) -> float:
     return lib().oracle_gelu_f64(x)
 

@@ -5,9 +5,9 @@
 // PAD floats of padding per row of the transposed A tile in shared memory.  Differences, for speed
 // on B200:
 //   * double-buffered shared memory with a register-staged prefetch of the next K step, so one
-//     barrier per K step instead of two;
+//     barrier per K step instead of two (tiles whose two stages exceed 48 KB keep one stage);
 //   * 16-byte global loads and stores; A is transposed on its way into shared memory;
-//   * when TM and TN are multiples of 4 a thread owns 4 x 4 sub-blocks spread BM/(TM/4) rows and
+//   * when TM and TN are multiples of 4 (and BM + PAD too, for A) a thread owns 4 x 4 sub-blocks spread BM/(TM/4) rows and
 //     BN/(TN/4) columns apart, so its shared-memory reads are conflict-free float4 loads;
 //   * ragged M / N / K are allowed (out-of-range loads read 0, stores are guarded).
 // Numerics match the reference kernel element for element: every C[r,c] is accumulated in fp32 by
@@ -29,13 +29,18 @@ struct SimtConfig {
   static constexpr int THREADS = (BM / TM) * (BN / TN);
   static constexpr int TX = BN / TN;  // threads along N
   static constexpr int TY = BM / TM;  // threads along M
-  static constexpr bool SPLIT_M = (TM % 4 == 0);
+  // float4 reads of the transposed A tile need 16-byte rows: BM + PAD a multiple of 4 floats.
+  static constexpr bool SPLIT_M = (TM % 4 == 0) && ((BM + PAD) % 4 == 0);
   static constexpr bool SPLIT_N = (TN % 4 == 0);
   static constexpr int A_VEC = BM * BK / 4;  // float4 pieces of the A tile
   static constexpr int B_VEC = BK * BN / 4;  // float4 pieces of the B tile
   static constexpr int A_PER = (A_VEC + THREADS - 1) / THREADS;
   static constexpr int B_PER = (B_VEC + THREADS - 1) / THREADS;
-  static constexpr int SMEM_BYTES = 2 * 4 * (BK * (BM + PAD) + BK * BN);
+  static constexpr int STAGE_BYTES = 4 * (BK * (BM + PAD) + BK * BN);
+  // Double-buffered when two stages fit the 48 KB of static shared memory, else one stage with two
+  // barriers per K step (as the reference kernel).  Either way every output is the same fmaf chain.
+  static constexpr int STAGES = 2 * STAGE_BYTES <= 48 * 1024 ? 2 : 1;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES;
   static_assert(BM % TM == 0 && BN % TN == 0, "tile not divisible by micro-tile");
   static_assert(BK % 4 == 0 && BN % 4 == 0, "BK and BN must be multiples of 4");
   static_assert(SMEM_BYTES <= 48 * 1024, "static shared memory above 48 KB");
@@ -58,8 +63,8 @@ __device__ __forceinline__ void gemm_bias_gelu_simt_body(const float *__restrict
                                                          const float *__restrict__ bias, float *__restrict__ C,
                                                          int M, int N, int K) {
   using Cfg = SimtConfig<BM, BN, BK, TM, TN, PAD>;
-  __shared__ __align__(16) float As[2][BK][BM + PAD];  // transposed: As[k][m]
-  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ __align__(16) float As[Cfg::STAGES][BK][BM + PAD];  // transposed: As[k][m]
+  __shared__ __align__(16) float Bs[Cfg::STAGES][BK][BN];
 
   const int tid = threadIdx.x;
   const int tx = tid % Cfg::TX;
@@ -148,7 +153,7 @@ __device__ __forceinline__ void gemm_bias_gelu_simt_body(const float *__restrict
   __syncthreads();
 
   for (int kt = 0; kt < ktiles; ++kt) {
-    const int buf = kt & 1;
+    const int buf = Cfg::STAGES == 2 ? (kt & 1) : 0;
     if (kt + 1 < ktiles) load_tiles((kt + 1) * BK);
 
 #pragma unroll
@@ -186,7 +191,10 @@ __device__ __forceinline__ void gemm_bias_gelu_simt_body(const float *__restrict
         for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
 
-    if (kt + 1 < ktiles) store_tiles(buf ^ 1);
+    if (kt + 1 < ktiles) {
+      if constexpr (Cfg::STAGES == 1) __syncthreads();  // every thread is done reading the one stage
+      store_tiles(Cfg::STAGES == 2 ? (buf ^ 1) : 0);
+    }
     __syncthreads();
   }
 

@@ -11,7 +11,9 @@ Writes
                        reference's source with the reference's own flags (tests/fake_cuda/run.sh:14).
   mt19937.npz          the first 2048 outputs of std::mt19937(99) (the generator of the reference gate's
                        sample positions, core/src/cuda_runner.cpp:190) and of std::mt19937(1234) (its
-                       input generator, cuda_runner.cpp:98), from a libstdc++ program compiled here.
+                       input generator, cuda_runner.cpp:98), from a libstdc++ program compiled here, and the
+                       first 2048 floats of std::uniform_real_distribution<float>(-0.5f, 0.5f) drawn from
+                       std::mt19937(1234) (the runner's input values, cuda_runner.cpp:98-102).
 
 The GPU box has no reference tree: tests read these files instead.
 """
@@ -34,11 +36,20 @@ CASES = [(64, 48, 40, 1), (96, 80, 72, 2), (128, 128, 128, 3), (33, 65, 129, 4)]
 
 MT_PROGRAM = r"""
 #include <cstdio>
+#include <cstring>
 #include <random>
 int main() {
   for (unsigned seed : {99u, 1234u}) {
     std::mt19937 g(seed);
     for (int i = 0; i < 2048; ++i) std::printf("%u\n", static_cast<unsigned>(g()));
+  }
+  std::mt19937 g(1234);
+  std::uniform_real_distribution<float> U(-0.5f, 0.5f);
+  for (int i = 0; i < 2048; ++i) {
+    const float v = U(g);
+    unsigned bits;
+    std::memcpy(&bits, &v, sizeof bits);
+    std::printf("%u\n", bits);
   }
 }
 """
@@ -64,7 +75,8 @@ def make_mt():
         subprocess.run(["g++", "-std=c++20", "-O1", src, "-o", exe], check=True)
         vals = np.array([int(x) for x in subprocess.run([exe], capture_output=True, text=True,
                                                          check=True).stdout.split()], dtype=np.uint32)
-    np.savez_compressed(os.path.join(HERE, "mt19937.npz"), seed99=vals[:2048], seed1234=vals[2048:])
+    np.savez_compressed(os.path.join(HERE, "mt19937.npz"), seed99=vals[:2048], seed1234=vals[2048:4096],
+                        uniform1234=vals[4096:6144].view(np.float32))
 
 
 if __name__ == "__main__":

@@ -200,7 +200,8 @@ def test_fp32_tile_outside_the_library_is_jit_compiled(tune_fake, tmp_path):
 
 
 def test_fp32_tile_that_does_not_compile_is_a_failed_trial(tune_fake, tmp_path):
-    # 2 x 4 x (32*(256+0) + 32*256) = 131 KB of static shared memory: nvcc refuses, the trial fails with its log
+    # one stage alone is 4 x (32*(256+0) + 32*256) = 64 KB of static shared memory (above 48 KB): nvcc refuses,
+    # the trial fails with its log
     args = ["measure", "--dtype", "f32", "--M", "256", "--N", "256", "--K", "64", "--BM", "256", "--BN", "256", "--BK",
             "32", "--TM", "16", "--TN", "16", "--PAD", "0", "--root", ROOT, "--workdir", str(tmp_path / "k")]
     r = run(tune_fake, args)
