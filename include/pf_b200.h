@@ -154,6 +154,13 @@ int pf_device_status(pf_ctx *ctx, unsigned *err_word);
  * order (deterministic for a given shape); the context keeps a workspace of 256 KB per CTA pair. */
 int pf_set_stream_k(pf_ctx *ctx, int mode);
 
+/* Row chunks of the host-buffer pipelines (pf_run_host, pf_run_host_rows): 0 = default (8), else at most
+ * `chunks` (1..64) chunks of whole kernel tiles, each one's copy of A in, kernel and copy of C out
+ * overlapping the others'.  More chunks shorten the pipeline's fill and drain (the first kernel starts
+ * after a smaller piece of A, the last copy of C is smaller) at the price of smaller launches.  The
+ * results do not depend on it: every chunk's tiles keep the whole problem's k order. */
+int pf_set_host_chunks(pf_ctx *ctx, int chunks);
+
 /* Bound, in nanoseconds, on every device-side wait of subsequent launches (default 4e9). */
 int pf_set_wait_timeout(pf_ctx *ctx, unsigned long long ns);
 

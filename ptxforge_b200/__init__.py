@@ -31,7 +31,7 @@ SYMBOLS = ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time
            "pf_device_status", "pf_set_wait_timeout", "pf_last_error", "pf_run_host", "pf_shard_rows",
            "pf_elem_bytes", "pf_out_bytes", "pf_version", "pf_selftest_wait_timeout", "pf_upload", "pf_download",
            "pf_gemm_bias_gelu_noalloc", "pf_prepare_image", "pf_time_cublas",
-           "pf_set_stream_k", "pf_run_host_rows")
+           "pf_set_stream_k", "pf_run_host_rows", "pf_set_host_chunks")
 
 
 class Tile(ctypes.Structure):
@@ -128,6 +128,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         dp = ctypes.POINTER(ctypes.c_double)
         lib.pf_time_cublas.argtypes = [vp, i, i, i, dp, dp]
         lib.pf_set_stream_k.argtypes = [vp, i]
+        lib.pf_set_host_chunks.argtypes = [vp, i]
         lib.pf_gemm_bias_gelu_noalloc.argtypes = [i, i, ctypes.POINTER(Tile), i, i, i, vp, vp, vp, vp, ctypes.c_float,
                                                   ctypes.c_float, vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p,
                                                   ctypes.c_size_t]
@@ -140,7 +141,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         for name in ("pf_open", "pf_close", "pf_prepare", "pf_bind", "pf_launch", "pf_time", "pf_attrs",
                      "pf_device_status", "pf_set_wait_timeout", "pf_run_host", "pf_run_host_rows", "pf_shard_rows",
                      "pf_selftest_wait_timeout", "pf_upload", "pf_download", "pf_gemm_bias_gelu_noalloc",
-                     "pf_prepare_image", "pf_time_cublas", "pf_set_stream_k"):
+                     "pf_prepare_image", "pf_time_cublas", "pf_set_stream_k", "pf_set_host_chunks"):
             getattr(lib, name).restype = ctypes.c_int
         if path is None:
             _lib = lib
@@ -261,6 +262,10 @@ class Context:
     def set_stream_k(self, mode: int):
         """Stream-K tail of the CTA-pair kernel: -1 auto (default), 0 off, 1 on (pf_set_stream_k)."""
         self._check(self._lib.pf_set_stream_k(self._h, mode), "pf_set_stream_k")
+
+    def set_host_chunks(self, chunks: int):
+        """Row chunks of the host-buffer pipelines: 0 default (8), else 1..64 (pf_set_host_chunks)."""
+        self._check(self._lib.pf_set_host_chunks(self._h, chunks), "pf_set_host_chunks")
 
     def set_wait_timeout(self, ns: int):
         self._check(self._lib.pf_set_wait_timeout(self._h, ns), "pf_set_wait_timeout")

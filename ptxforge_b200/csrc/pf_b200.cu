@@ -332,6 +332,7 @@ struct pf_ctx {
 
   // stream-K tail of the CTA-pair kernel: mode (-1 auto, 0 off, 1 on), launch epoch, workspace, flags
   int stream_k = -1;
+  int host_chunks = 0;   // pf_set_host_chunks: 0 = default
   unsigned epoch = 0;
   float *sk_ws = nullptr;
   unsigned *sk_flags = nullptr;
@@ -673,6 +674,12 @@ int pf_set_stream_k(pf_ctx *c, int mode) {
   return PF_OK;
 }
 
+int pf_set_host_chunks(pf_ctx *c, int chunks) {
+  if (!c || chunks < 0 || chunks > 64) return set_err(c, PF_EINVAL, "host chunks must be 0 (default) or 1..64");
+  c->host_chunks = chunks;
+  return PF_OK;
+}
+
 int pf_set_wait_timeout(pf_ctx *c, unsigned long long ns) {
   if (!c || ns == 0) return set_err(c, PF_EINVAL, "timeout must be positive");
   c->timeout_ns = ns;
@@ -912,6 +919,9 @@ int ensure_host_bufs(pf_ctx *c, float sa, float sb) {
   return PF_OK;
 }
 
+// Row chunks of the host-buffer pipelines.
+int host_chunk_cap(const pf_ctx *c) { return c->host_chunks > 0 ? c->host_chunks : 8; }
+
 // Launch the bound problem restricted to output rows [r0, r0 + rows) on stream s: the same kernel
 // variant on row windows of A and C (TMA maps re-encoded for the window on the tensor path).
 int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
@@ -988,7 +998,7 @@ int pf_run_host(pf_ctx *c, const void *hA, const void *hB, const float *hbias, v
   // kernels overlap).  An image keeps its fixed launch shape: one chunk.
   const int align = c->var.path == Path::kTensor ? c->var.bm : c->var.path == Path::kSimt ? c->var.sbm : c->M;
   const int units = (c->M + align - 1) / align;
-  const int P = c->var.path == Path::kImage ? 1 : std::max(1, std::min(8, units));
+  const int P = c->var.path == Path::kImage ? 1 : std::max(1, std::min(host_chunk_cap(c), units));
   if (!c->s_comp) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_comp, cudaStreamNonBlocking));
   if (!c->s_out) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
   while (c->ev_pool.size() < static_cast<size_t>(2 * P + 1)) {
@@ -1033,7 +1043,7 @@ int pf_run_host_rows(pf_ctx *c, const void *hA, void *hC, void *after_stream, vo
   const size_t rowA = static_cast<size_t>(c->K) * e, rowC = static_cast<size_t>(c->N) * o;
   const int align = c->var.path == Path::kTensor ? c->var.bm : c->var.sbm;
   const int units = (c->M + align - 1) / align;
-  const int P = std::max(1, std::min(8, units));
+  const int P = std::max(1, std::min(host_chunk_cap(c), units));
   if (!c->s_comp) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_comp, cudaStreamNonBlocking));
   if (!c->s_out) PF_CUDA(c, cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
   while (c->ev_pool.size() < static_cast<size_t>(2 * P + 1)) {

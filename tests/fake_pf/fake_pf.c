@@ -93,6 +93,8 @@ int pf_set_wait_timeout(pf_ctx *c, unsigned long long ns) { return (!c || !ns) ?
 
 int pf_set_stream_k(pf_ctx *c, int mode) { return (!c || mode < -1 || mode > 1) ? PF_EINVAL : PF_OK; }
 
+int pf_set_host_chunks(pf_ctx *c, int chunks) { return (!c || chunks < 0 || chunks > 64) ? PF_EINVAL : PF_OK; }
+
 int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
   if (!c || !t) return PF_EINVAL;
   flog("prepare", c->device);

@@ -322,6 +322,27 @@ def test_pipelined_host_path_equals_device_path(ctx, name, shape, tile):
     assert np.array_equal(hC, want)
 
 
+@pytest.mark.parametrize("chunks", [1, 3, 16, 64])
+def test_host_chunks_do_not_change_the_result(ctx, pf, chunks):
+    # pf_set_host_chunks: any number of row chunks gives the single launch's bits (stream-K off on the
+    # single launch: 256 tiles are 3.5 waves, where the auto tail would split the last tiles' k range)
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 4096, 4096, 512)
+    inp = wl.make_inputs(w, seed=19)
+    ctx.set_stream_k(0)
+    try:
+        C = run_pf(ctx, w, inp)
+        hC = np.empty((w.M, w.N), dtype=np.uint16)
+        ctx.prepare(w.dtype, None, w.M, w.N, w.K)
+        ctx.set_host_chunks(chunks)
+        ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC)
+    finally:
+        ctx.set_host_chunks(0)
+        ctx.set_stream_k(-1)
+    assert np.array_equal(hC, C.view(torch.int16).cpu().numpy().view(np.uint16))
+    with pytest.raises(pf.PFError):
+        ctx.set_host_chunks(65)
+
+
 # ---------------------------------------------------------------------------------------------
 # stream-K tail of the CTA-pair kernel
 # ---------------------------------------------------------------------------------------------
