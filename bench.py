@@ -58,6 +58,15 @@ def parse_args():
     return ap.parse_args()
 
 
+def l2_note(w) -> str:
+    """How the timed steps stand to the 126 MB L2 (no flush between steps either way)."""
+    mb = w.algorithmic_bytes() / 1e6
+    if mb > 126:
+        return f"no flush: A+B+C ({mb:.0f} MB) exceed the 126 MB L2"
+    return (f"no flush: A+B+C ({mb:.1f} MB) fit in the 126 MB L2, so steps re-read cached operands, as back-to-back "
+            "launches of the reference protocol (median_ms) do")
+
+
 def host_threads() -> int:
     """Every host core this process may run on (torchrun sets OMP_NUM_THREADS=1; the CPU legs ignore it)."""
     try:
@@ -392,7 +401,7 @@ def run_ours(args, dist):
             "distributions)",
             "config": {"workload": w.name, "M": w.M, "N": w.N, "K": w.K, "rows_per_gpu": rows,
                        "tile": list(tile), "parallelism": f"M-rows x{dist.world}, B+bias replicated, no "
-                       "collective", "l2": "no flush: A+B+C exceed the 126 MB L2",
+                       "collective", "l2": l2_note(w),
                        "global_batch": w.M, "seq_len": None},
             "pct_of_peak": round(100.0 * value / (peak * dist.world), 2) if peak else None,
             "roofline": {"bound": "tensor" if w.dtype != "f32" else "fp32-simt", "achieved": round(achieved, 2),

@@ -197,6 +197,10 @@ const SimtEntry kSimtTable[] = {
     {{64, 64, 16, 4, 4, 4}, &make_simt_variant<64, 64, 16, 4, 4, 4>},
     {{32, 64, 8, 2, 4, 4}, &make_simt_variant<32, 64, 8, 2, 4, 4>},
     {{32, 32, 8, 2, 2, 0}, &make_simt_variant<32, 32, 8, 2, 2, 0>},
+    // small problems (fewer 128 x 128 tiles than SMs): the best of a 160-trial tune at 512^3 on B200
+    {{32, 32, 32, 4, 2, 2}, &make_simt_variant<32, 32, 32, 4, 2, 2>},
+    {{64, 32, 32, 4, 2, 2}, &make_simt_variant<64, 32, 32, 4, 2, 2>},
+    {{32, 64, 32, 4, 2, 2}, &make_simt_variant<32, 64, 32, 4, 2, 2>},
 };
 
 bool same_tile(const pf_tile &a, const pf_tile &b) {

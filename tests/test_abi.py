@@ -80,3 +80,8 @@ def test_default_tile_choice_follows_the_measurements():
     for rows, N in [(1024, 8192), (2048, 8192), (4096, 14336), (8192, 8192), (16384, 14336)]:
         assert pf.default_tile("bf16", rows, N) == pf.DEFAULT_TILES["bf16"], (rows, N)
     assert pf.default_tile("f32", 2048, 2048) == pf.DEFAULT_TILES["f32"]
+    # fp32 SIMT (same bits on every tile): small tiles while the 128 x 128 default would leave SMs idle
+    assert pf.default_tile("f32", 512, 512) == (32, 32, 32, 4, 2, 2)
+    assert pf.default_tile("f32", 1024, 1024) == (64, 64, 16, 4, 4, 4)
+    assert pf.default_tile("f32", 1536, 1536) == pf.DEFAULT_TILES["f32"]
+    assert pf.default_tile("f32_3xtf32", 512, 512) == pf.DEFAULT_TILES["f32_3xtf32"]
