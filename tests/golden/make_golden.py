@@ -1,6 +1,6 @@
 """Generate the golden fixtures in tests/golden/ from the reference's own code.
 
-Run in a container where the reference tree is mounted (default /root/reference):
+Run where the reference tree is mounted (its root in $PTXFORGE_REFERENCE, default as in oracle/build.py):
 
     python tests/golden/make_golden.py
 
