@@ -147,9 +147,10 @@ int pf_attrs(pf_ctx *ctx, pf_attr *out);
  * bit 2: epilogue wait, bit 3: teardown wait, bit 4: 3xTF32 split wait). */
 int pf_device_status(pf_ctx *ctx, unsigned *err_word);
 
-/* Stream-K tail of the CTA-pair (BM=256) kernel: -1 auto (default: used with at least 3 waves of tiles
- * when the last partial wave would waste more than 3 % of the launch), 0 off (every tile whole: results independent of the
- * launch shape, bit for bit), 1 on whenever there is a partial wave.  With the tail, the leftover tiles'
+/* Stream-K tail of the CTA-pair (BM=256) kernels: -1 auto (default: with at least 3 waves of tiles when the
+ * last partial wave would waste more than 3 % of the launch; PF_F32_3XTF32 also below that when whole tiles
+ * would leave a quarter of the CTA pairs idle, given 4 leftover k-blocks per pair), 0 off (every tile whole:
+ * results independent of the launch shape, bit for bit), 1 on whenever there is a partial wave.  With the tail, the leftover tiles'
  * k-iterations are spread over all resident CTA pairs and their fp32 partial sums added in a fixed
  * order (deterministic for a given shape); the context keeps a workspace of 256 KB per CTA pair. */
 int pf_set_stream_k(pf_ctx *ctx, int mode);

@@ -32,6 +32,9 @@
 //               TMEM columns) goes back to the MMA lane right after its last load.
 // Separate rings let TMA run ahead of the MMAs (a raw slot is free once split, not once multiplied) and
 // let the split write without waiting for its own reads of the slot to finish elsewhere in the block.
+// Work units are those of the CTA-pair kernel (sk_unit, gemm_tc2.cuh): whole tiles, then, with a stream-K
+// tail, contiguous k ranges of the last tiles spread over every pair; a tail tile's head pair adds the other
+// pairs' fp32 partial sums in its epilogue.  k always ascends inside a unit.
 #pragma once
 
 #include "gemm_tc2.cuh"
@@ -64,7 +67,8 @@ struct Tf32x3Config {
   static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 4;    // 32 rows x 128 B
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 2 * RAW_STAGES + 2 * SPLIT_STAGES + 4 + 1;
+  static constexpr int NUM_BARS = 2 * RAW_STAGES + 2 * SPLIT_STAGES + 4 + 1 + 1;
+  static constexpr int PARTIAL_FLOATS = BM_CTA * BN;         // one CTA's share of a tile, fp32
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES =
       1024 + SPLIT_STAGES * SPLIT_BYTES + RAW_STAGES * RAW_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
@@ -121,7 +125,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   uint64_t *tfull = split_empty + Cfg::SPLIT_STAGES;      // [2] both: accumulator ready
   uint64_t *tempty = tfull + 2;                           // [2] leader: both CTAs drained the accumulator
   uint64_t *drain = tempty + 2;                           // [1] leader: all MMAs complete
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *epi_sync = drain + 1;                         // [1] the 4 epilogue warps wrote this worker's partial
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_sync + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -147,6 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       mbar_init(&tempty[a], 2 * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(epi_sync, Cfg::EPI_WARPS);        // completes at most once: a worker has at most one partial
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -172,12 +178,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int issued = 0;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      SkUnit un;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
         int mb, nb;
-        tile_coords(t, p, mb, nb);
+        tile_coords(un.tile, p, mb, nb);
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&raw_empty[slot], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
@@ -229,8 +236,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     int rslot = 0, sslot = 0;
     uint32_t rphase = 0, sphase = 0;
     bool ok = true;
-    for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+    SkUnit un;
+    for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
+      for (int kb = un.kb0; kb < un.kb1; ++kb) {
         // 1. the raw slot's bytes, into registers
         bool waited = mbar_wait(&raw_full[rslot], rphase, p.timeout_ns, abort_flag);
         if (!__all_sync(0xffffffffu, waited)) {
@@ -299,7 +307,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      SkUnit un;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
           ok = false;
@@ -307,7 +316,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
           if (!mbar_wait_cluster(&ready[sslot], sphase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
@@ -324,7 +333,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             const uint64_t bh = smem_desc(b_hi + k * 32, 16, 1024, kSwizzle128B);
             const uint64_t bl = smem_desc(b_lo + k * 32, 16, 1024, kSwizzle128B);
             // small terms first
-            tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, (i | k) != 0 ? 1u : 0u);
             tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
             tc_mma_tf32_pair(d_tmem, ah, bh, Cfg::IDESC, 1u);
           }
@@ -353,9 +362,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int buf = 0;
-    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+    SkUnit un;
+    // This CTA's partial-sum slot (its 128 rows of a tile) in worker `w`'s workspace; a warp's 32 rows are
+    // stored quad-of-columns-major so one warp-wide 16-byte access covers 512 contiguous bytes.
+    auto slot = [&](int w) -> float4 * {
+      return reinterpret_cast<float4 *>(p.sk_partials + (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
+                                        static_cast<size_t>(q) * 32 * Cfg::BN);
+    };
+    for (int u = 0; sk_unit(pair, num_pairs, u, p, un); ++u) {
       int mb, nb;
-      tile_coords(t, p, mb, nb);
+      tile_coords(un.tile, p, mb, nb);
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
@@ -365,40 +381,107 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
       const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[acc]), 0);
+      if (un.kind == kUnitPartial) {
+        // Write this worker's fp32 partial (its k range of the tile) and raise its flag.
+        float4 *dst = slot(pair);
 #pragma unroll 1
-      for (int c = 0; c < Cfg::BN / Cfg::EPI_COLS; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS, v);
-        tmem_ld_wait();
-        if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
-          // Last TMEM read of this accumulator: hand it back to the MMA issuer.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty_leader);
-        }
-        const int n0 = nb * Cfg::BN + c * Cfg::EPI_COLS;
-        const uint32_t sbuf = smem_u32(ebuf + buf * Cfg::EPI_BUF_BYTES) + lane * 128;
+        for (int c = 0; c < Cfg::BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
-          const float y0 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 0]) + b4.x);
-          const float y1 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 1]) + b4.y);
-          const float y2 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 2]) + b4.z);
-          const float y3 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 3]) + b4.w);
-          // row `lane` of the 32 x 32 fp32 box: 16-byte chunk j4 goes to chunk j4 ^ (row % 8)
-          st_shared_v4(sbuf + static_cast<uint32_t>((j4 ^ (lane & 7)) * 16), __float_as_uint(y0), __float_as_uint(y1),
-                       __float_as_uint(y2), __float_as_uint(y3));
+          for (int j4 = 0; j4 < 8; ++j4)
+            __stcg(dst + (c * 8 + j4) * 32 + lane,
+                   make_float4(__uint_as_float(v[j4 * 4 + 0]), __uint_as_float(v[j4 * 4 + 1]),
+                               __uint_as_float(v[j4 * 4 + 2]), __uint_as_float(v[j4 * 4 + 3])));
         }
-        fence_proxy_async_smem();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, ebuf + buf * Cfg::EPI_BUF_BYTES, n0, m0);
-          tma_store_commit();
-          tma_store_wait_read<1>();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader);
+        // Every warp's stores are visible device-wide before it arrives; one lane publishes the flag once all
+        // four have arrived (bounded wait, never a hardware barrier a departed warp could block).
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_sync);
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait(epi_sync, 0, p.timeout_ns, abort_flag))
+            st_release_gpu(p.sk_flags + pair * 2 + rank, p.epoch);
+          else
+            fail(kErrEpilogueWait);
         }
-        __syncwarp();
-        buf ^= 1;
+      } else {
+        // Whole tile, or the head of a tail tile: add the later workers' partials (bounded waits).
+        int first = 0, last = -1;
+        if (un.kind == kUnitHead) {
+          const long long tile_end = static_cast<long long>(un.tile - p.dp_tiles + 1) * p.k_blocks;
+          first = pair + 1;
+          last = pair;
+          while (last + 1 < num_pairs && sk_start(last + 1, num_pairs, p) < tile_end) ++last;
+          bool ok = true;
+          if (lane == 0) {
+            for (int w = first; w <= last && ok; ++w) {
+              const unsigned *flag = p.sk_flags + w * 2 + rank;
+              if (ld_acquire_gpu(flag) != p.epoch) {
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_gpu(flag) != p.epoch) {
+                  if (*abort_flag || globaltimer_ns() - t0 > p.timeout_ns) {
+                    ok = false;
+                    break;
+                  }
+                  __nanosleep(256);
+                }
+              }
+            }
+            if (!ok) fail(kErrEpilogueWait);
+          }
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        }
+#pragma unroll 1
+        for (int c = 0; c < Cfg::BN / Cfg::EPI_COLS; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS, v);
+          tmem_ld_wait();
+          if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
+            // Last TMEM read of this accumulator: hand it back to the MMA issuer.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader);
+          }
+          for (int w = first; w <= last; ++w) {
+            const float4 *src = slot(w) + c * 8 * 32 + lane;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 s4 = __ldcg(src + j4 * 32);
+              v[j4 * 4 + 0] = __float_as_uint(__uint_as_float(v[j4 * 4 + 0]) + s4.x);
+              v[j4 * 4 + 1] = __float_as_uint(__uint_as_float(v[j4 * 4 + 1]) + s4.y);
+              v[j4 * 4 + 2] = __float_as_uint(__uint_as_float(v[j4 * 4 + 2]) + s4.z);
+              v[j4 * 4 + 3] = __float_as_uint(__uint_as_float(v[j4 * 4 + 3]) + s4.w);
+            }
+          }
+          const int n0 = nb * Cfg::BN + c * Cfg::EPI_COLS;
+          const uint32_t sbuf = smem_u32(ebuf + buf * Cfg::EPI_BUF_BYTES) + lane * 128;
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
+            const float y0 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 0]) + b4.x);
+            const float y1 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 1]) + b4.y);
+            const float y2 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 2]) + b4.z);
+            const float y3 = gelu_tanh_exp(__uint_as_float(v[j4 * 4 + 3]) + b4.w);
+            // row `lane` of the 32 x 32 fp32 box: 16-byte chunk j4 goes to chunk j4 ^ (row % 8)
+            st_shared_v4(sbuf + static_cast<uint32_t>((j4 ^ (lane & 7)) * 16), __float_as_uint(y0),
+                         __float_as_uint(y1), __float_as_uint(y2), __float_as_uint(y3));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, ebuf + buf * Cfg::EPI_BUF_BYTES, n0, m0);
+            tma_store_commit();
+            tma_store_wait_read<1>();
+          }
+          __syncwarp();
+          buf ^= 1;
+        }
       }
       if (++acc == 2) {
         acc = 0;

@@ -52,6 +52,12 @@ struct Variant {
   int katoms = 1;               // 128-byte k-atoms per pipeline stage
   int cta_per_tile = 1;         // 2 = CTA-pair (cluster) kernel
   bool stream_k = false;        // the kernel can run a stream-K tail
+  // Auto stream-K (pf_set_stream_k -1): at least this many waves of tiles (with a partial last one), or whole
+  // tiles keeping fewer than this fraction of the workers busy; and at least this many of the leftover tiles'
+  // k-blocks per worker.
+  double sk_min_waves = 3.0;
+  double sk_low_util = 0.0;
+  int sk_min_share = 1;
   int b_chunk_n = 0;
   // (grid, stream, A map, B map, C map, C tail map -- used by tiles whose width is not a multiple of 64)
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
@@ -152,6 +158,12 @@ Variant make_tf32x3_variant() {
   v.a_box_k = Cfg::ATOM_K;
   v.katoms = 1;
   v.cta_per_tile = 2;
+  // Below 3 waves the tail pays once whole tiles would leave a quarter of the pairs idle: measured (us, off ->
+  // on) 16 tiles 86.3 -> 50.1, 32 tiles 86.5 -> 60.5, 36 tiles 76.2 -> 60.6, but 64 tiles 87.6 -> 89.9 (the
+  // partial writes, the head's wait and its reads cost ~12 us per launch).
+  v.stream_k = true;
+  v.sk_low_util = 0.75;
+  v.sk_min_share = 4;
   v.launch_tc = &launch_tf32x3_impl<RAW, SPLIT>;
   return v;
 }
@@ -452,7 +464,10 @@ int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
   if (R == 0 || static_cast<long long>(R) * k_blocks < W) return 0;
   if (c->stream_k < 0) {
     const double waves = static_cast<double>(tiles) / W;
-    if (waves < 3.0 || std::ceil(waves) / waves < 1.03) return 0;
+    const bool many_waves = waves >= c->var.sk_min_waves && std::ceil(waves) / waves >= 1.03;
+    const bool idle_workers = tiles / (std::ceil(waves) * W) < c->var.sk_low_util;
+    if (!many_waves && !idle_workers) return 0;
+    if (static_cast<long long>(R) * k_blocks < static_cast<long long>(c->var.sk_min_share) * W) return 0;
   }
   return R;
 }

@@ -138,10 +138,37 @@ def test_attrs_and_timing(ctx):
     inp = wl.make_inputs(w)
     run(ctx, w, inp)
     a = ctx.attrs()
-    assert a["threads"] == 448 and a["local_bytes"] <= 16 and a["grid"] == 2 * 64  # 8 x 8 tiles, one pair each
+    # 8 x 8 tiles for 74 pairs keep 86 % of them busy: whole tiles, one pair each (auto stream-K stays off)
+    assert a["threads"] == 448 and a["local_bytes"] <= 16 and a["grid"] == 2 * 64
     ms = ctx.time(warmup=3, iters=10, reps=3)
     assert 0 < ms < 5.0
     assert ctx.status() == 0
+    # 4 x 4 tiles would keep 22 % busy: the auto tail spreads their k-blocks over every pair
+    w2 = workload(1024, 1024, 2048)
+    run(ctx, w2, wl.make_inputs(w2))
+    assert ctx.attrs()["grid"] == 148
+
+
+@pytest.mark.parametrize("shape", [(2048, 2048, 2048), (513, 264, 1028), (300, 1000, 1000), (1536, 1536, 1536)])
+def test_stream_k_tail_vs_fp64_and_whole_tiles(ctx, oracle_mod, shape):
+    # The stream-K tail (forced on) splits tiles' k ranges between pairs and adds their fp32 partials:
+    # within the tolerance of fp64, within a few fp32 roundings of the whole-tile result, deterministic.
+    w = workload(*shape)
+    inp = wl.make_inputs(w, seed=29)
+    ops = operands(inp, w.M, w.N)
+    ctx.set_stream_k(1)
+    try:
+        sk = run(ctx, w, inp, None, ops).clone()
+        assert ctx.attrs()["grid"] == 148
+        again = run(ctx, w, inp, None, ops).clone()
+        ctx.set_stream_k(0)
+        whole = run(ctx, w, inp, None, ops).clone()
+    finally:
+        ctx.set_stream_k(-1)
+    assert torch.equal(sk, again)
+    assert full_err(oracle_mod, inp, sk) <= TOL
+    d = ((sk.double() - whole.double()).abs() / (1 + whole.double().abs())).max().item()
+    assert d <= 2 * TOL
 
 
 def test_cublas_comparator_for_the_fp32_path(ctx):
