@@ -18,6 +18,8 @@ Besides the device-timed `value`, the line carries
   comparators   cuBLAS GEMM alone and cuBLAS + a separate bias+GELU pass (pf_time_cublas), same inputs
   cpu_baseline  the CPU-lowered schedule (oracle port) on the host cores, on a bounded sample (N=1)
   clocks        SM clock and throttle reasons sampled (NVML) during the timed region
+  energy        this GPU's energy per step over the timed region (NVML total-energy counter): under the
+                ~1 kW power cap the clock, and so the throughput, follows energy per launch
 `--impl reference` times the reference's CPU implementation of the path (the port of its CPU-lowered
 schedule, all host threads) on the same workload and prints the same line with "impl": "reference".
 """
@@ -136,8 +138,16 @@ class ClockSampler:
                 pass
             time.sleep(self.interval)
 
+    def _energy(self):
+        try:
+            return self.nv.nvmlDeviceGetTotalEnergyConsumption(self.h)  # mJ since the driver loaded
+        except Exception:
+            return None
+
     def __enter__(self):
+        self.e0 = self.e1 = None
         if self.ok:
+            self.e0 = self._energy()
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
         return self
@@ -146,6 +156,14 @@ class ClockSampler:
         if self.ok:
             self._stop.set()
             self.t.join()
+            self.e1 = self._energy()
+
+    def energy(self, steps: int):
+        """Energy of this GPU per step over the timed region (NVML's total-energy counter)."""
+        if self.e0 is None or self.e1 is None or steps <= 0:
+            return {"mj_per_step": None, "source": "nvml total energy counter (unavailable)"}
+        return {"mj_per_step": round((self.e1 - self.e0) / steps, 1),
+                "source": "nvml total energy counter, this rank's GPU, over the timed region"}
 
     def summary(self):
         if not self.ok or not self.samples:
@@ -242,7 +260,7 @@ def run_ours(args, dist):
     r0, rows = pf.shard_rows(w.M, dist.world, dist.rank, 128)
     A, B, bias, C = device_operands(torch, w, inp, r0, rows)
     scale = inp.scale_a * inp.scale_b
-    tile = tuple(int(x) for x in args.tile.split(",")) if args.tile else pf.default_tile(w.dtype, rows, w.N)
+    tile = tuple(int(x) for x in args.tile.split(",")) if args.tile else pf.default_tile(w.dtype, rows, w.N, w.K)
     ctx = pf.Context(dist.local_rank)
     ctx.prepare(w.dtype, tile, rows, w.N, w.K)
     ctx.bind(A, B, bias, C, inp.scale_a, inp.scale_b)
@@ -419,6 +437,7 @@ def run_ours(args, dist):
             "gpu_launches": args.steps,
             "gate": {"max_rel_err": gate_err, "tolerance": w.tolerance, "samples": 256},
             "clocks": clk.summary(),
+            "energy": clk.energy(args.steps),
             "kernel": {"attrs": attrs},
         }
         if c_gather:

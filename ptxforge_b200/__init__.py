@@ -64,22 +64,28 @@ DEFAULT_TILES = {
     "bf16": (256, 256, 32, 8, 16, 1),
     "e4m3": (256, 256, 32, 8, 16, 1),
 }
+# 256 x 512 CTA-pair tiles, 3 stages, 8 epilogue warps (gemm_tc2w.cuh); default_tile picks them for long tiles.
+WIDE_TILE = (256, 512, 32, 3, 16, 0)
 
 
-def default_tile(dtype: str, rows: int, N: int, pairs: int = 74) -> tuple:
-    """The best-measured tile for a rows x N output on one GPU (what prepare() uses when given no tile).
+def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int = 74) -> tuple:
+    """The best-measured tile for a rows x N x K problem on one GPU (what prepare() uses when given no tile).
 
-    bf16 / e4m3 use CTA-pair tiles 256 rows high and, as a rule, 256 columns wide.  A 224-wide pair tile
-    measured about as slow per tile as a 256-wide one (its B rows start 224 / 112 bytes into a 128-byte line),
-    so it only pays where the 256-wide schedule's last wave of tiles is nearly empty and 224-wide tiles add no
-    wave: MLP shards of 2048 x 14336 (448 tiles, 4 in the last wave of 74 pairs) ran 6 % faster with 224;
-    8192-column shards of 1024 / 2048 rows and MLP shards of 4096 rows ran 1.6-3.7 % slower.
+    bf16 / e4m3: CTA-pair tiles 256 rows high.  256 x 512 tiles with 8 epilogue warps (WIDE_TILE) move a quarter
+    fewer operand bytes through L2 per output and, under the power cap, ran faster where tiles are long and
+    their waves full: sustained 8192^3 bf16 +1 %, 16384^3 e4m3 +4.9 %, both with less energy per launch; with
+    64 k steps per tile (the 4096-deep MLP) they lost 3 %, and on row shards whose 512-wide tiles leave a
+    partial wave the 256-wide kernel's stream-K tail is ahead.  So: 512-wide from 128 k steps per tile when
+    at least 95 % of the last wave is full.  Otherwise 256 columns, or 224 where the 256-wide schedule's last
+    wave is nearly empty and 224-wide tiles add no wave: MLP shards of 2048 x 14336 (448 tiles, 4 in the last
+    wave of 74 pairs) ran 6 % faster with 224; 8192-column shards of 1024 / 2048 rows and MLP shards of 4096
+    rows ran 1.6-3.7 % slower.
+    f32: the SIMT kernel gives the same bits on every tile; small problems get small tiles.
     """
     base = DEFAULT_TILES[dtype]
     if dtype == "f32":
-        # The SIMT kernel gives the same bits on every tile; the 128 x 128 default only fills the GPU from about
-        # 128 of its tiles.  Measured (TFLOP/s, n^3): 512: 14.4 on 32 x 32 vs 4.0; 1024: 26.8 on 64 x 64 vs 16.8;
-        # 1536: 39.1 on 128 x 128 vs 34.3 on 64 x 64.
+        # The 128 x 128 default only fills the GPU from about 128 of its tiles.  Measured (TFLOP/s, n^3):
+        # 512: 14.4 on 32 x 32 vs 4.0; 1024: 26.8 on 64 x 64 vs 16.8; 1536: 39.1 on 128 x 128 vs 34.3 on 64 x 64.
         t128 = -(-rows // 128) * -(-N // 128)
         if t128 < 48:
             return (32, 32, 32, 4, 2, 2)
@@ -88,6 +94,11 @@ def default_tile(dtype: str, rows: int, N: int, pairs: int = 74) -> tuple:
         return base
     if dtype not in ("bf16", "e4m3") or base[0] != 256:
         return base
+    if K is not None:
+        k_steps = -(-K // (64 if dtype == "bf16" else 128))
+        t512 = -(-rows // 256) * -(-N // 512)
+        if k_steps >= 128 and t512 >= 0.95 * (-(-t512 // pairs) * pairs):
+            return WIDE_TILE
     t256 = -(-rows // 256) * -(-N // 256)
     t224 = -(-rows // 256) * -(-N // 224)
     tail = t256 % pairs
@@ -226,7 +237,7 @@ class Context:
         self.close()
 
     def prepare(self, dtype: str, tile, M: int, N: int, K: int):
-        t = tile if isinstance(tile, Tile) else Tile(*(tile or default_tile(dtype, M, N)))
+        t = tile if isinstance(tile, Tile) else Tile(*(tile or default_tile(dtype, M, N, K)))
         self._check(self._lib.pf_prepare(self._h, DTYPES[dtype], ctypes.byref(t), M, N, K), "pf_prepare")
         self.dtype, self.shape, self.tile = dtype, (M, N, K), t
         return self

@@ -197,7 +197,8 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n_tile + c * EPI_COLS, m0);
+      // A box wholly right of C (a 512-wide tile's columns past a ragged N) stores nothing.
+      if (n_tile + c * EPI_COLS < p.N) tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n_tile + c * EPI_COLS, m0);
       tma_store_commit();
       tma_store_wait_read<1>();  // the other buffer is free again
     }

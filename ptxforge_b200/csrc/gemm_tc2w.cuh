@@ -1,0 +1,357 @@
+// gemm_tc2w.cuh -- the fused GEMM + bias + GELU on CTA pairs with 256 x 512 tiles.
+//
+// Per k step a pair of the 256 x 256 kernel (gemm_tc2.cuh) loads 256 rows of A and 256 columns of B for
+// 65,536 outputs; a pair here loads 256 rows of A and 512 columns of B for 131,072 outputs: a quarter
+// fewer operand bytes through L2 per output.  Under back-to-back launches the B200 runs at its power
+// cap, so those bytes cost clock, not just bandwidth.
+//
+// Each CTA's 128 accumulator rows x 512 fp32 columns fill its TMEM, so there is one accumulator per CTA,
+// handed back in two halves: the epilogue drains columns [0, 256) and releases them, and the next
+// tile's MMAs into that half start while it drains [256, 512).  The MMA issuer runs a stage's second-half
+// MMAs as soon as that half is free; until then it holds at most STAGES stages whose second half is
+// still to do (their shared memory stays loaded), and waits only when all of them are held.
+//   * TMA (both CTAs): per stage, A rows [m0 + 128*rank, +128) and, for each half h, B columns
+//     [n0 + 256*h + 128*rank, +128), counted on the leader's `full` barrier (no multicast);
+//   * MMA (leader lane): per stage and half h, tcgen05.mma.cta_group::2 with M = 256, N = 256 into TMEM
+//     columns [256*h, 256*h + 256); tcgen05.commit multicasts stage-free and accumulator-ready;
+//   * epilogue (kEpiWarps warps from warp 2, both CTAs): the 256-wide kernel's epilogue, one half at a time,
+//     each half released to the leader's `tempty[h]` right after its last TMEM load.  With 8 warps two
+//     share each 32-lane quarter of TMEM and split a half's 256 columns, so a half drains in about half the
+//     time: the tensor pipe waits on that drain at every tile boundary.
+// Whole tiles only (no stream-K tail); the k direction alternates by wave as in the other kernels.
+#pragma once
+
+#include "gemm_tc2.cuh"
+
+namespace pf {
+
+template <int kDtype, int kStages, int kEpiWarps = 4>
+struct Tc2wConfig {
+  static constexpr int BM = 256;                             // pair tile rows
+  static constexpr int BM_CTA = 128;
+  static constexpr int BN = 512;                             // pair tile columns
+  static constexpr int HALF_N = 256;                         // UMMA N of each half
+  static constexpr int STAGES = kStages;
+  static constexpr int ELEM = (kDtype == 0) ? 2 : 1;
+  static constexpr int KATOMS = 1;                           // one 128-byte k-atom per stage
+  static constexpr int ATOM_K = 128 / ELEM;
+  static constexpr int BK = ATOM_K;
+  static constexpr int UMMA_K = 32 / ELEM;
+  static constexpr int A_BYTES = BM_CTA * 128;
+  static constexpr int B_CHUNK_N = 128 / ELEM;               // N elements per 128-byte row of B
+  static constexpr int B_CHUNKS_HALF = (HALF_N / 2) / B_CHUNK_N;  // boxes per CTA and half
+  static constexpr int B_CHUNK_BYTES = BK * 128;
+  static constexpr int B_HALF_BYTES = B_CHUNKS_HALF * B_CHUNK_BYTES;
+  static constexpr int B_BYTES = 2 * B_HALF_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // per CTA
+  static constexpr int EPI_WARPS = kEpiWarps;                // 4 or 8: 1 or 2 per 32-lane quarter of TMEM
+  static constexpr int EPI_SPLIT = kEpiWarps / 4;            // warps sharing a quarter split its columns
+  static constexpr int EPI_COLS_WARP = HALF_N / EPI_SPLIT;   // columns of a half each epilogue warp drains
+  static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
+  static constexpr int EPI_BUFS = 2;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1;
+  static constexpr int TMEM_COLS = 512;                      // one accumulator: two halves of 256 columns
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr uint32_t IDESC =
+      instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ HALF_N);
+  static_assert(kEpiWarps == 4 || kEpiWarps == 8, "4 or 8 epilogue warps");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
+  static_assert(B_CHUNKS_HALF >= 1, "each CTA supplies at least one 128-byte box of B per half");
+};
+
+// One epilogue warp's 32 rows x 128 columns of one accumulator half: the four 32-column TMEM loads first,
+// then the half is handed back (`release`) before any epilogue math, which runs from registers while the
+// next tile's MMAs already write that half; then x*scale + bias, GELU, bf16, two 32 x 64 boxes through the
+// double-buffered swizzled staging area and TMA stores, as epilogue_rows.
+template <class Release>
+__device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, int n0, const TcParams &p,
+                                                       const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
+                                                       Release release) {
+  constexpr int BUF_BYTES = 32 * 64 * 2;
+  uint32_t v[4][32];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_col + c * 32, v[c]);
+  tmem_ld_wait();
+  tc_fence_before();
+  __syncwarp();
+  release();
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 128;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t packed[16];
+      epilogue_math32(v[b * 2 + h], n0 + b * 64 + h * 32, p, packed);
+      // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t chunk = static_cast<uint32_t>((h * 4 + i) ^ (lane & 7));
+        st_shared_v4(sbuf + chunk * 16, packed[i * 4 + 0], packed[i * 4 + 1], packed[i * 4 + 2], packed[i * 4 + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (n0 + b * 64 < p.N) tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n0 + b * 64, m0);
+      tma_store_commit();
+      tma_store_wait_read<1>();  // the other buffer is free again
+    }
+    __syncwarp();
+    buf ^= 1;
+  }
+}
+
+template <class Cfg>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
+    gemm_bias_gelu_tc2w(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + Cfg::STAGES * Cfg::A_BYTES;
+  uint8_t *sEpi = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + Cfg::EPI_BYTES);
+  uint64_t *full = bars;                        // [STAGES] leader: TMA bytes of both CTAs landed
+  uint64_t *empty = bars + Cfg::STAGES;         // [STAGES] both: MMAs reading the stage finished
+  uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [1] both: accumulator ready
+  uint64_t *tempty = tfull + 1;                 // [2] leader: both CTAs drained half h
+  uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();      // 0 = leader, 1 = follower
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);                   // the leader's producer arrives (with both CTAs' bytes)
+      mbar_init(&empty[s], 1);                  // one multicast commit
+    }
+    mbar_init(tfull, 1);
+    mbar_init(&tempty[0], 2 * Cfg::EPI_WARPS);
+    mbar_init(&tempty[1], 2 * Cfg::EPI_WARPS);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+    tc_fence_before();
+  }
+  // Both CTAs' barriers are initialised before any remote arrive or TMA completion targets them.
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  auto fail = [&](unsigned bit) {
+    atomicOr(p.status, bit);
+    *abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
+        const int n0 = nb * Cfg::BN + static_cast<int>(rank) * (Cfg::HALF_N / 2);
+        const bool reversed = tile_k_reversed(p, mb, nb, num_pairs);
+        for (int i = 0; i < p.k_blocks; ++i) {
+          const int kb = reversed ? p.k_blocks - 1 - i : i;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
+            fail(kErrProducerWait);
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const uint32_t bar = pair_leader_addr(smem_u32(&full[stage]));
+          tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * Cfg::BK, m0);
+          uint8_t *b_dst = sB + stage * Cfg::B_BYTES;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < Cfg::B_CHUNKS_HALF; ++j)
+              tma_load_2d_pair(b_dst + h * Cfg::B_HALF_BYTES + j * Cfg::B_CHUNK_BYTES, &tmB, bar,
+                               n0 + h * Cfg::HALF_N + j * Cfg::B_CHUNK_N, kb * Cfg::BK);
+          ++issued;
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Let loads already in flight land before the pair may exit (bounded).
+        for (int s = 0; s < Cfg::STAGES && s < issued; ++s) {
+          const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+          volatile int no_abort = 0;
+          if (!mbar_wait(&full[s], ph, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t tphase = 0;  // parity of this pair's tile count: the halves are released once per tile
+      bool ok = true;
+      const uint32_t tempty1_addr = smem_u32(&tempty[1]);
+      // Half h's MMAs of the stage in ring slot s, the tile's i-th k step.
+      auto issue_half = [&](int s, int h, int i) {
+        const uint32_t a_addr = smem_u32(sA + s * Cfg::A_BYTES);
+        const uint32_t b_addr = smem_u32(sB + s * Cfg::B_BYTES + h * Cfg::B_HALF_BYTES);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(h * Cfg::HALF_N);
+#pragma unroll
+        for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+          const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+          const uint64_t bd = smem_desc(b_addr + k * Cfg::UMMA_K * 128, Cfg::B_CHUNK_BYTES, 1024, kSwizzle128B);
+          const uint32_t accumulate = (i != 0 || k != 0) ? 1u : 0u;
+          if constexpr (Cfg::ELEM == 2)
+            tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, accumulate);
+          else
+            tc_mma_f8_pair(d_tmem, ad, bd, Cfg::IDESC, accumulate);
+        }
+      };
+      // The second half of the `pending` most recent stages (the last in slot `last`, k step i_last),
+      // oldest first, each stage handed back to the producers once its second half is issued.
+      auto flush = [&](int pending, int last, int i_last) {
+        for (int j = pending - 1; j >= 0; --j) {
+          const int s = (last - j + Cfg::STAGES) % Cfg::STAGES;
+          issue_half(s, 1, i_last - j);
+          tc_commit_pair_mc(&empty[s], 0x3);
+        }
+      };
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        // The first half of the accumulator must be drained of the previous tile.
+        if (!mbar_wait_cluster(&tempty[0], tphase ^ 1u, p.timeout_ns, abort_flag)) {
+          fail(kErrMmaWait);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bool second_free = false;
+        int pending = 0;  // stages whose second-half MMAs wait for the second half of TMEM
+        int last = 0;
+        for (int i = 0; i < p.k_blocks; ++i) {
+          if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
+            fail(kErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_half(stage, 0, i);
+          ++pending;
+          last = stage;
+          if (!second_free && mbar_test_wait_acq_cluster(tempty1_addr, tphase ^ 1u)) {
+            second_free = true;
+            tc_fence_after();
+          }
+          if (!second_free && pending == Cfg::STAGES) {
+            // Every stage is held: nothing more can load until the second half is free.
+            if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
+              fail(kErrMmaWait);
+              ok = false;
+              break;
+            }
+            second_free = true;
+            tc_fence_after();
+          }
+          if (second_free) {
+            flush(pending, last, i);
+            pending = 0;
+          }
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (pending > 0) {
+          // A tile of fewer k steps than stages: its second half waits here.
+          if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
+            fail(kErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          flush(pending, last, p.k_blocks - 1);
+        }
+        tc_commit_pair_mc(tfull, 0x3);
+        tphase ^= 1u;
+      }
+      tc_commit_pair(drain);
+      volatile int no_abort = 0;
+      if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2.., both CTAs)
+    const int q = warp & 3;                     // the TMEM lane quarter this warp may read
+    const int ew = warp - 2;
+    const int col0 = (ew / 4) * Cfg::EPI_COLS_WARP;  // its columns within each half
+    uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;
+    uint32_t tphase = 0;
+    int buf = 0;
+    const uint32_t tempty0_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty1_leader = mapa_shared(smem_u32(&tempty[1]), 0);
+    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const bool waited = mbar_wait(tfull, tphase, p.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, waited)) {
+        if (lane == 0) fail(kErrEpilogueWait);
+        break;
+      }
+      tc_fence_after();
+      const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      auto release0 = [&] {
+        if (lane == 0) mbar_arrive_cluster(tempty0_leader);
+      };
+      auto release1 = [&] {
+        if (lane == 0) mbar_arrive_cluster(tempty1_leader);
+      };
+      if constexpr (Cfg::EPI_COLS_WARP == 128) {
+        // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
+        epilogue_rows128_early(t_row + col0, m0, nb * Cfg::BN + col0, p, &tmC, ebuf, buf, lane, release0);
+        epilogue_rows128_early(t_row + Cfg::HALF_N + col0, m0, nb * Cfg::BN + Cfg::HALF_N + col0, p, &tmC, ebuf, buf,
+                               lane, release1);
+      } else {
+        epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, nb * Cfg::BN + col0, p, &tmC, nullptr, ebuf, buf, lane,
+                                          release0);
+        epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, m0, nb * Cfg::BN + Cfg::HALF_N + col0, p, &tmC,
+                                          nullptr, ebuf, buf, lane, release1);
+      }
+      tphase ^= 1u;
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  // Neither CTA releases TMEM or exits while its peer may still address it.
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace pf

@@ -22,6 +22,7 @@
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tc2w.cuh"
 #include "gemm_tf32x3.cuh"
 
 #ifndef PF_VERSION_STR
@@ -128,6 +129,36 @@ Variant make_tc2_variant() {
   v.cta_per_tile = 2;
   v.stream_k = true;
   v.launch_tc = &launch_tc2_impl<DT, ST, KA, BN>;
+  return v;
+}
+
+template <int DT, int ST, int EW>
+void launch_tc2w_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                      const CUtensorMap &, const TcParams &p) {
+  using Cfg = pf::Tc2wConfig<DT, ST, EW>;
+  pf::gemm_bias_gelu_tc2w<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+}
+
+// CTA pairs with 256 x 512 tiles (gemm_tc2w.cuh): whole tiles, one k-atom per stage.
+template <int DT, int ST, int EW>
+Variant make_tc2w_variant() {
+  using Cfg = pf::Tc2wConfig<DT, ST, EW>;
+  Variant v;
+  v.path = Path::kTensor;
+  v.func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_tc2w<Cfg>);
+  v.threads = Cfg::THREADS;
+  v.smem = Cfg::SMEM_BYTES;
+  v.bm = Cfg::BM;
+  v.bn = Cfg::BN;
+  v.bk_elems = Cfg::BK;
+  v.stages = Cfg::STAGES;
+  v.elem = Cfg::ELEM;
+  v.b_chunk_n = Cfg::B_CHUNK_N;
+  v.a_box_rows = Cfg::BM_CTA;
+  v.a_box_k = Cfg::ATOM_K;
+  v.katoms = Cfg::KATOMS;
+  v.cta_per_tile = 2;
+  v.launch_tc = &launch_tc2w_impl<DT, ST, EW>;
   return v;
 }
 
@@ -240,6 +271,9 @@ bool find_tc_variant(pf_dtype dt, int bm, int bn, int depth, int katoms, Variant
       {PF_E4M3, 256, 256, 4, 1, &make_tc2_variant<1, 4>},         {PF_E4M3, 256, 256, 6, 1, &make_tc2_variant<1, 6>},
       {PF_E4M3, 256, 256, 3, 2, &make_tc2_variant<1, 3, 2>},
       {PF_BF16, 256, 224, 3, 2, &make_tc2_variant<0, 3, 2, 224>}, {PF_E4M3, 256, 224, 3, 2, &make_tc2_variant<1, 3, 2, 224>},
+      // 256 x 512: 3 stages with 8 epilogue warps, 4 stages with 4 (shared memory holds one or the other)
+      {PF_BF16, 256, 512, 3, 1, &make_tc2w_variant<0, 3, 8>},      {PF_E4M3, 256, 512, 3, 1, &make_tc2w_variant<1, 3, 8>},
+      {PF_BF16, 256, 512, 4, 1, &make_tc2w_variant<0, 4, 4>},      {PF_E4M3, 256, 512, 4, 1, &make_tc2w_variant<1, 4, 4>},
       {PF_F32_3XTF32, 256, 256, 2, 1, &make_tf32x3_variant<1, 1>},
       {PF_F32_3XTF32, 256, 256, 3, 1, &make_tf32x3_variant<1, 2>},
       {PF_F32_3XTF32, 256, 256, 4, 1, &make_tf32x3_variant<2, 2>},

@@ -254,6 +254,20 @@ __device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar_addr, uin
   return ok != 0;
 }
 
+// Non-blocking probe of a barrier phase that other CTAs of the cluster arrive on (acquire at cluster scope):
+// returns at once, where try_wait may suspend the thread for a while first.
+__device__ __forceinline__ bool mbar_test_wait_acq_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on a barrier that other CTAs of the cluster arrive on (acquire at cluster scope).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, uint64_t timeout_ns,
                                                   volatile int *abort_flag) {

@@ -33,7 +33,7 @@ class ShardedHostGemm:
         self.M, self.N, self.K = M, N, K
         self.scale_a, self.scale_b = scale_a, scale_b
         self.r0, self.rows = shard_span(M, ranks.world, ranks.rank, tuple(tile or DEFAULT_TILES[dtype])[0])
-        tile = tuple(tile) if tile else default_tile(dtype, self.rows, N)
+        tile = tuple(tile) if tile else default_tile(dtype, self.rows, N, K)
         e, o = ELEM_BYTES[dtype], OUT_BYTES[dtype]
         self.kslice = -(-K // ranks.world)                      # rows of B each rank brings in
         dev = torch.device("cuda", ranks.local_rank)

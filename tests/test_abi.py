@@ -80,6 +80,12 @@ def test_default_tile_choice_follows_the_measurements():
     for rows, N in [(1024, 8192), (2048, 8192), (4096, 14336), (8192, 8192), (16384, 14336)]:
         assert pf.default_tile("bf16", rows, N) == pf.DEFAULT_TILES["bf16"], (rows, N)
     assert pf.default_tile("f32", 2048, 2048) == pf.DEFAULT_TILES["f32"]
+    # 256 x 512 tiles for long tiles whose waves are full (1 GPU); the 256-wide kernel elsewhere
+    assert pf.default_tile("bf16", 8192, 8192, 8192) == pf.WIDE_TILE          # 512 tiles, 128 k steps
+    assert pf.default_tile("e4m3", 16384, 16384, 16384) == pf.WIDE_TILE       # 2048 tiles, 128 k steps
+    assert pf.default_tile("bf16", 16384, 14336, 4096) == pf.DEFAULT_TILES["bf16"]   # 64 k steps
+    for rows in (1024, 2048, 4096):  # row shards of 8192^3: 512-wide tiles would leave 13.5 % of a wave idle
+        assert pf.default_tile("bf16", rows, 8192, 8192) == pf.DEFAULT_TILES["bf16"], rows
     # fp32 SIMT (same bits on every tile): small tiles while the 128 x 128 default would leave SMs idle
     assert pf.default_tile("f32", 512, 512) == (32, 32, 32, 4, 2, 2)
     assert pf.default_tile("f32", 1024, 1024) == (64, 64, 16, 4, 4, 4)

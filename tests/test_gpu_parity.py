@@ -377,13 +377,13 @@ def test_stream_k_tail_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape, b
         ctx.set_stream_k(-1)
 
 
-def test_stream_k_forced_at_full_size(ctx, oracle_mod):
+def test_stream_k_forced_at_full_size(ctx, oracle_mod, pf):
     w = wl.CONFIGS["cfg3_bf16_8192"]
     inp = wl.make_inputs(w)
     A, B, bias, C = device_operands(w, inp)
     ctx.set_stream_k(1)
     try:
-        run_pf(ctx, w, inp, None, (A, B, bias, C))
+        run_pf(ctx, w, inp, pf.DEFAULT_TILES["bf16"], (A, B, bias, C))  # the 256-wide kernel (stream-K tail)
     finally:
         ctx.set_stream_k(-1)
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
@@ -404,6 +404,67 @@ def test_224_wide_tiles_on_row_shards(ctx, oracle_mod, pf, name, rows):
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
     assert err <= TOL[ws.dtype]
     assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[ws.dtype]
+
+
+# ---------------------------------------------------------------------------------------------
+# 256 x 512 pair tiles (gemm_tc2w.cuh): one accumulator per CTA, handed back in two halves
+# ---------------------------------------------------------------------------------------------
+WIDE = (256, 512, 32, 4, 16, 0)      # 4 stages, 4 epilogue warps
+WIDE8 = (256, 512, 32, 3, 16, 0)     # 3 stages, 8 epilogue warps (two per TMEM lane quarter)
+
+
+@pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (512, 1024, 512)),
+                                        ("cfg3_bf16_8192", (600, 1000, 1000)),   # ragged; last half partly past N
+                                        ("cfg3_bf16_8192", (300, 520, 264)),     # boxes wholly past N
+                                        ("cfg3_bf16_8192", (256, 512, 64)),      # one k step, fewer than the stages
+                                        ("cfg3_bf16_8192", (4096, 8192, 256)),   # 3.5 tiles per pair, 4 k steps each
+                                        ("cfg5_e4m3_16384", (1024, 2048, 1024)),
+                                        ("cfg5_e4m3_16384", (600, 1008, 1008)),  # e4m3 rows: 16-byte multiples
+                                        ("cfg5_e4m3_16384", (4096, 8192, 384))])
+@pytest.mark.parametrize("tile", [WIDE, WIDE8])
+def test_512_wide_tiles_vs_oracle_and_256_wide(ctx, oracle_mod, name, shape, tile):
+    w = wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w, seed=43)
+    A, B, bias, C = device_operands(w, inp)
+    run_pf(ctx, w, inp, tile, (A, B, bias, C))
+    assert ctx.attrs()["threads"] == (192 if tile == WIDE else 320)
+    assert ctx.attrs()["grid"] == 2 * min(74, -(-w.M // 256) * -(-w.N // 512))
+    if w.M * w.N * w.K <= 2 ** 30:
+        check_full(oracle_mod, w, inp, C)
+    else:
+        err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), inp.scale_a * inp.scale_b, samples=512,
+                                            seed=99)
+        assert err <= TOL[w.dtype]
+    again = torch.full_like(C, float("nan"))
+    run_pf(ctx, w, inp, tile, (A, B, bias, again))
+    assert torch.equal(C, again)
+    narrow = torch.full_like(C, float("nan"))
+    run_pf(ctx, w, inp, None, (A, B, bias, narrow))
+    assert max_rel_err_t(narrow.float(), C.float()) <= TOL[w.dtype]
+
+
+@pytest.mark.parametrize("name", ["cfg3_bf16_8192", "cfg4_bf16_mlp"])
+@pytest.mark.parametrize("tile", [WIDE, WIDE8])
+def test_512_wide_tiles_at_full_size(ctx, oracle_mod, name, tile):
+    w = wl.CONFIGS[name]
+    inp = wl.make_inputs(w)
+    A, B, bias, C = device_operands(w, inp)
+    run_pf(ctx, w, inp, tile, (A, B, bias, C))
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= TOL[w.dtype]
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[w.dtype]
+
+
+@pytest.mark.parametrize("tile", [WIDE, WIDE8])
+def test_512_wide_tiles_host_path_equals_device_path(ctx, tile):
+    # row chunks of 512-wide tiles keep the whole launch's k order: the same bits
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 4096, 4096, 512)
+    inp = wl.make_inputs(w, seed=47)
+    C = run_pf(ctx, w, inp, tile)
+    hC = np.empty((w.M, w.N), dtype=np.uint16)
+    ctx.prepare(w.dtype, tile, w.M, w.N, w.K)
+    ctx.run_host(inp.A_raw, inp.B_raw, inp.bias, hC)
+    assert np.array_equal(hC, C.view(torch.int16).cpu().numpy().view(np.uint16))
 
 
 @pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (2048, 1024, 768)), ("cfg5_e4m3_16384", (1000, 512, 512)),
