@@ -58,7 +58,9 @@ typedef enum {
 /* The tuner's tile config: exactly the fields of ptxforge::Config (core/include/ptxforge/space.hpp:58).
  *   fp32 path   : the reference meaning (block tile BM x BN, K step BK, TM x TN per thread, PAD).
  *   tensor path : BM = tile rows: 128 (one CTA, UMMA M=128) or 256 (a CTA pair, cta_group::2);
- *                 BN = UMMA N (64/128/256; 256 for BM=256); BK = 32 (4-byte words of one 128-byte
+ *                 BN = UMMA N (64/128/256) for BM=128; for BM=256 the pair tile's columns: 256, 224, or
+ *                 512 (two N=256 halves in one TMEM accumulator: TM=3 gives 8 epilogue warps, TM>=4 four,
+ *                 PAD=0); BK = 32 (4-byte words of one 128-byte
  *                 swizzle row); TM = requested pipeline depth in stages (clamped to the deepest
  *                 compiled variant that fits shared memory); TN = tile-raster group height in M
  *                 blocks (consecutive tiles walk TN row blocks before moving along N); PAD = extra
