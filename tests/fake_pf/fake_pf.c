@@ -104,10 +104,11 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     if (t->BM != 128 && t->BM != 256) return set_err(c, PF_ETILE, "tensor path: BM must be 128 or 256, got %d", t->BM);
     if (t->BK != 32) return set_err(c, PF_ETILE, "tensor path: BK must be 32 words, got %d", t->BK);
     if (t->PAD != 0 && t->PAD != 1) return set_err(c, PF_ETILE, "tensor path: PAD must be 0 or 1, got %d", t->PAD);
-    if (!(t->BN == 256 || t->BN == 128 || (t->BN == 64 && dt == PF_BF16) || (t->BN == 224 && t->BM == 256)) ||
-        (t->BM == 256 && t->BN != 256 && t->BN != 224))
+    if (!(t->BN == 256 || t->BN == 128 || (t->BN == 64 && dt == PF_BF16) || ((t->BN == 224 || t->BN == 512) && t->BM == 256)) ||
+        (t->BM == 256 && t->BN != 256 && t->BN != 224 && t->BN != 512))
       return set_err(c, PF_ETILE, "tensor path: no kernel with BM=%d BN=%d", t->BM, t->BN);
-    if (t->TM < 2) return set_err(c, PF_ETILE, "tensor path: no kernel with %d stages", t->TM);
+    if (t->TM < (t->BN == 512 ? 3 : 2)) return set_err(c, PF_ETILE, "tensor path: no kernel with %d stages", t->TM);
+    if (t->BN == 512 && t->PAD != 0) return set_err(c, PF_ETILE, "tensor path: 512-column tiles take one k-atom");
     const int e = (int)pf_elem_bytes(dt);
     if ((K * e) % 16 || (N * e) % 16 || (N * 2) % 16) return set_err(c, PF_ESHAPE, "rows must be multiples of 16 bytes");
   } else if (dt == PF_F32) {
@@ -115,7 +116,8 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     static const int known[][6] = {{128, 128, 8, 8, 8, 4}, {128, 128, 8, 8, 8, 0}, {128, 128, 16, 8, 8, 4},
                                    {128, 64, 8, 8, 4, 4},  {64, 128, 8, 4, 8, 4},  {64, 64, 8, 4, 4, 0},
                                    {64, 64, 8, 4, 4, 4},   {64, 64, 16, 4, 4, 4},  {32, 64, 8, 2, 4, 4},
-                                   {32, 32, 8, 2, 2, 0}};
+                                   {32, 32, 8, 2, 2, 0},   {32, 32, 32, 4, 2, 2},  {64, 32, 32, 4, 2, 2},
+                                   {32, 64, 32, 4, 2, 2}};
     int found = 0;
     for (size_t i = 0; i < sizeof known / sizeof known[0]; ++i)
       found |= known[i][0] == t->BM && known[i][1] == t->BN && known[i][2] == t->BK && known[i][3] == t->TM &&

@@ -95,6 +95,17 @@ def test_unmappable_config_is_a_failed_trial(tune_fake):
     assert rc == 4 and not j["ok"] and "BM must be" in j["error"]
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "e4m3"])
+def test_512_column_pair_tiles(tune_fake, dtype):
+    # 256 x 512 pair tiles: one k-atom per stage (PAD 0), at least 3 stages; PAD >= 1 asks for two k-atoms,
+    # which no 512-wide kernel has: a failed trial, never a crash
+    wide = ["--BM", "256", "--BN", "512", "--BK", "32", "--TM", "3", "--TN", "16"]
+    rc, j, _ = measure(tune_fake, ["--dtype", dtype, *wide, "--PAD", "0"])
+    assert rc == 0 and j["ok"], j
+    rc, j, _ = measure(tune_fake, ["--dtype", dtype, *wide, "--PAD", "1"])
+    assert rc == 4 and not j["ok"] and "k-atom" in j["error"]
+
+
 def test_bk_and_pad_are_canonical_on_the_tensor_path(tune_fake):
     rc, j, _ = measure(tune_fake, ["--BM", "128", "--BN", "128", "--BK", "8", "--TM", "4", "--TN", "8", "--PAD", "2"])
     assert rc == 0 and j["ok"]
