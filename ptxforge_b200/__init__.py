@@ -72,11 +72,13 @@ def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int
     """The best-measured tile for a rows x N x K problem on one GPU (what prepare() uses when given no tile).
 
     bf16 / e4m3: CTA-pair tiles 256 rows high.  256 x 512 tiles with 8 epilogue warps (WIDE_TILE) move a quarter
-    fewer operand bytes through L2 per output and, under the power cap, ran faster where tiles are long and
-    their waves full: sustained 8192^3 bf16 +1 %, 16384^3 e4m3 +4.9 %, both with less energy per launch; with
-    64 k steps per tile (the 4096-deep MLP) they lost 3 %, and on row shards whose 512-wide tiles leave a
-    partial wave the 256-wide kernel's stream-K tail is ahead.  So: 512-wide from 128 k steps per tile when
-    at least 95 % of the last wave is full.  Otherwise 256 columns, or 224 where the 256-wide schedule's last
+    fewer operand bytes through L2 per output and, under the power cap, ran faster with long tiles: sustained
+    8192^3 bf16 +1 %, 16384^3 e4m3 +4.9 %, both with less energy per launch; with 64 k steps per tile (the
+    4096-deep MLP) they lost 3 %.  On row shards of 8192^3 (rows x 8192 x 8192) they won at 1,024 and 2,048 rows
+    (+3 %, +0.9 %: there both widths leave the same share of the last wave idle, and idle SMs free power for
+    the busy ones) and lost at 4,096 rows (-3.8 %: 256 x 512 tiles fill 86.5 % of their waves, 256 x 256 ones
+    98.8 %).  So: 512-wide from 128 k steps per tile when their wave fill is within 2 points of the 256-wide
+    kernel's.  Otherwise 256 columns, or 224 where the 256-wide schedule's last
     wave is nearly empty and 224-wide tiles add no wave: MLP shards of 2048 x 14336 (448 tiles, 4 in the last
     wave of 74 pairs) ran 6 % faster with 224; 8192-column shards of 1024 / 2048 rows and MLP shards of 4096
     rows ran 1.6-3.7 % slower.
@@ -94,12 +96,14 @@ def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int
         return base
     if dtype not in ("bf16", "e4m3") or base[0] != 256:
         return base
+    t256 = -(-rows // 256) * -(-N // 256)
     if K is not None:
         k_steps = -(-K // (64 if dtype == "bf16" else 128))
         t512 = -(-rows // 256) * -(-N // 512)
-        if k_steps >= 128 and t512 >= 0.95 * (-(-t512 // pairs) * pairs):
+        fill512 = t512 / (-(-t512 // pairs) * pairs)
+        fill256 = t256 / (-(-t256 // pairs) * pairs)
+        if k_steps >= 128 and fill512 >= fill256 - 0.02:
             return WIDE_TILE
-    t256 = -(-rows // 256) * -(-N // 256)
     t224 = -(-rows // 256) * -(-N // 224)
     tail = t256 % pairs
     if 0 < tail <= pairs // 10 and -(-t224 // pairs) <= -(-t256 // pairs):

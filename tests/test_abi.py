@@ -84,8 +84,12 @@ def test_default_tile_choice_follows_the_measurements():
     assert pf.default_tile("bf16", 8192, 8192, 8192) == pf.WIDE_TILE          # 512 tiles, 128 k steps
     assert pf.default_tile("e4m3", 16384, 16384, 16384) == pf.WIDE_TILE       # 2048 tiles, 128 k steps
     assert pf.default_tile("bf16", 16384, 14336, 4096) == pf.DEFAULT_TILES["bf16"]   # 64 k steps
-    for rows in (1024, 2048, 4096):  # row shards of 8192^3: 512-wide tiles would leave 13.5 % of a wave idle
-        assert pf.default_tile("bf16", rows, 8192, 8192) == pf.DEFAULT_TILES["bf16"], rows
+    # row shards of 8192^3: 512-wide where both widths fill their waves alike (1,024 and 2,048 rows), 256-wide
+    # where 512-wide tiles would fill 86.5 % against 98.8 % (4,096 rows)
+    assert pf.default_tile("bf16", 1024, 8192, 8192) == pf.WIDE_TILE
+    assert pf.default_tile("bf16", 2048, 8192, 8192) == pf.WIDE_TILE
+    assert pf.default_tile("bf16", 4096, 8192, 8192) == pf.DEFAULT_TILES["bf16"]
+    assert pf.default_tile("e4m3", 2048, 16384, 16384) == pf.DEFAULT_TILES["e4m3"]  # 3.5 vs 6.9 waves
     # fp32 SIMT (same bits on every tile): small tiles while the 128 x 128 default would leave SMs idle
     assert pf.default_tile("f32", 512, 512) == (32, 32, 32, 4, 2, 2)
     assert pf.default_tile("f32", 1024, 1024) == (64, 64, 16, 4, 4, 4)
