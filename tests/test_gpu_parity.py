@@ -455,6 +455,21 @@ def test_512_wide_tiles_at_full_size(ctx, oracle_mod, name, tile):
     assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[w.dtype]
 
 
+@pytest.mark.parametrize("rows", [1024, 2048])
+def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
+    # the 8- and 4-GPU row shards of config 3, where default_tile picks 256 x 512 tiles
+    w = wl.CONFIGS["cfg3_bf16_8192"]
+    ws = wl.scaled(w, rows, w.N, w.K)
+    assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == pf.WIDE_TILE
+    inp = wl.make_inputs(ws, seed=53)
+    A, B, bias, C = device_operands(ws, inp)
+    run_pf(ctx, ws, inp, None, (A, B, bias, C))
+    assert ctx.attrs()["threads"] == 320
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= TOL[ws.dtype]
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[ws.dtype]
+
+
 @pytest.mark.parametrize("tile", [WIDE, WIDE8])
 def test_512_wide_tiles_host_path_equals_device_path(ctx, tile):
     # row chunks of 512-wide tiles keep the whole launch's k order: the same bits
