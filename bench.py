@@ -8,6 +8,8 @@ launch of the fused kernel over the whole problem; with N GPUs (one process each
 rows of M are split across the ranks (B and bias replicated, no collective on the data path) and the
 step time is the max over ranks of each rank's CUDA-event time (strong scaling: the 8192^3 problem is
 fixed).  FLOPs are 2*M*N*K (the epilogue is not counted, as in the reference, space.hpp:55).
+`--shard-of G` times, on one GPU, the row shard that rank 0 of a G-GPU run gets (value = that GPU's
+TFLOP/s): the per-GPU half of a scaling measurement at 1/G of its GPU time.
 
 Besides the device-timed `value`, the line carries
   e2e           the same metric end to end from pinned host buffers, every step: at N=1 the C ABI's
@@ -57,6 +59,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparators", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample budget")
+    ap.add_argument("--shard-of", type=int, default=0, metavar="G",
+                    help="on one GPU, time rank 0's row shard of a G-GPU run instead of the whole problem "
+                         "(a development measurement: value is then that one GPU's TFLOP/s)")
     return ap.parse_args()
 
 
@@ -257,7 +262,10 @@ def run_ours(args, dist):
     w = wl.CONFIGS[args.config]
     torch.cuda.set_device(dist.local_rank)
     inp = wl.make_inputs(w)
-    r0, rows = pf.shard_rows(w.M, dist.world, dist.rank, 128)
+    if args.shard_of and dist.world != 1:
+        raise SystemExit("--shard-of times one shard on one GPU: run it without torchrun")
+    shards = args.shard_of if args.shard_of else dist.world
+    r0, rows = pf.shard_rows(w.M, shards, dist.rank, 128)
     A, B, bias, C = device_operands(torch, w, inp, r0, rows)
     scale = inp.scale_a * inp.scale_b
     tile = tuple(int(x) for x in args.tile.split(",")) if args.tile else pf.default_tile(w.dtype, rows, w.N, w.K)
@@ -388,7 +396,7 @@ def run_ours(args, dist):
     res = None
     if dist.rank == 0:
         pk, pk_kind = peaks()
-        total_flops = w.flops
+        total_flops = w.flops if not args.shard_of else 2.0 * rows * w.N * w.K
         value = total_flops / (ms * 1e-3) / 1e12
         per_gpu_flops = 2.0 * rows * w.N * w.K
         achieved = per_gpu_flops / (ms_local * 1e-3) / 1e12
@@ -411,13 +419,14 @@ def run_ours(args, dist):
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
             with open(tp) as f:
-                traffic = json.load(f).get(f"{w.name}@{dist.world}")
+                traffic = json.load(f).get(f"{w.name}@{shards}")
         res = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded, BASELINE "
             "distributions)",
             "config": {"workload": w.name, "M": w.M, "N": w.N, "K": w.K, "rows_per_gpu": rows,
+                       **({"shard_of": args.shard_of} if args.shard_of else {}),
                        "tile": list(tile), "parallelism": f"M-rows x{dist.world}, B+bias replicated, no "
                        "collective", "l2": l2_note(w),
                        "global_batch": w.M, "seq_len": None},

@@ -43,7 +43,9 @@ def _max_rel_err(ref, C):
 CASES = [("cfg3_bf16_8192", (128, 256, 32, 4, 16, 0), (512, 768, 640)),
          ("cfg3_bf16_8192", (256, 256, 32, 8, 16, 0), (512, 768, 640)),
          ("cfg3_bf16_8192", (128, 256, 32, 4, 16, 0), (200, 136, 72)),
-         ("cfg5_e4m3_16384", (128, 256, 32, 4, 16, 0), (384, 512, 768))]
+         ("cfg5_e4m3_16384", (128, 256, 32, 4, 16, 0), (384, 512, 768)),
+         ("cfg3_bf16_8192", (256, 512, 32, 3, 16, 0), (512, 1024, 640)),   # 256 x 512 pair tiles
+         ("cfg5_e4m3_16384", (256, 512, 32, 3, 16, 0), (384, 1024, 768))]
 
 
 @pytest.mark.parametrize("name,tile,shape", CASES)
