@@ -484,6 +484,7 @@ def test_512_wide_tiles_host_path_equals_device_path(ctx, tile):
 
 @pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (2048, 1024, 768)), ("cfg5_e4m3_16384", (1000, 512, 512)),
                                         ("cfg3_bf16_8192", (4096, 4096, 512)),
+                                        ("cfg3_bf16_8192", (2048, 4096, 8192)),  # default: 256 x 512 tiles
                                         ("cfg2_f32_2048", (1030, 256, 128))])
 def test_run_host_rows_equals_device_path(ctx, name, shape):
     # pf_run_host_rows: B and bias already on the device (bound); host rows of A in, C rows out, in chunks
@@ -495,6 +496,8 @@ def test_run_host_rows_equals_device_path(ctx, name, shape):
         run_pf(ctx, w, inp, None, (A, B, bias, C))
         A2, C2 = torch.zeros_like(A), torch.full_like(C, float("nan"))
         ctx.prepare(w.dtype, None, w.M, w.N, w.K)
+        if shape == (2048, 4096, 8192):
+            assert ctx.tile.BN == 512  # the 4- and 8-GPU e2e path's tiles
         ctx.bind(A2, B, bias, C2, inp.scale_a, inp.scale_b)
         hA = torch.from_numpy(np.ascontiguousarray(inp.A_raw)).pin_memory()
         hC = torch.empty(C.numel() * C.element_size(), dtype=torch.uint8).pin_memory()
