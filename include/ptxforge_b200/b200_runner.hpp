@@ -110,16 +110,27 @@ class B200Runner : public Runner {
 
   std::string source() const override { return "harness"; }
 
+  // Whether a tensor-path Config asks for the 256 x 512 pair tiles (see to_tile).
+  static bool wide(const Config &c) { return c.BM == 256 && c.BN == 256 && (c.PAD == 2 || c.PAD == 4); }
+
   // The tuner's Config onto a pf_tile.  On the tensor-core path the k-block is made of 128-byte swizzle
   // atoms, so BK has no counterpart and is set to 32, and PAD (shared-memory padding in the SIMT kernel)
-  // selects one (PAD=0) or two (PAD>=1) k-atoms per stage; every (BM, BN, TM, TN) the search proposes
-  // then reaches a kernel when one exists.  BM, BN, TM and TN keep the meaning pf_b200.h gives them.
-  // The fp32 path takes the Config as it is.
+  // selects the stage layout: PAD=0 one k-atom per stage, PAD=1 or 8 two.  The search domain's columns
+  // stop at 256 (space.hpp: BN in {32, 64, 128, 256}), so the 256 x 512 pair tiles are reached through
+  // BM=256, BN=256 with PAD=2 (8 epilogue warps, 3 stages) or PAD=4 (4 epilogue warps, 4 stages); every
+  // (BM, BN, TM, TN) the search proposes then reaches a kernel when one exists.  BM, BN, TM and TN keep the
+  // meaning pf_b200.h gives them otherwise.  The fp32 path takes the Config as it is.
   pf_tile to_tile(const Config &c) const {
     pf_tile t{c.BM, c.BN, c.BK, c.TM, c.TN, c.PAD};
     if (opt_.dtype == PF_BF16 || opt_.dtype == PF_E4M3) {
       t.BK = 32;
-      t.PAD = c.PAD >= 1 ? 1 : 0;
+      if (wide(c)) {
+        t.BN = 512;
+        t.TM = c.PAD == 2 ? 3 : 4;
+        t.PAD = 0;
+      } else {
+        t.PAD = c.PAD >= 1 ? 1 : 0;
+      }
     } else if (opt_.dtype == PF_F32_3XTF32) {
       t.BK = 32;
       t.PAD = 0;
@@ -292,6 +303,7 @@ class B200Runner : public Runner {
     const bool tensor = opt_.dtype == PF_BF16 || opt_.dtype == PF_E4M3;
     const std::string file = opt_.dtype == PF_F32_3XTF32 ? "gemm_tf32x3.cuh"
                              : !tensor                   ? "gemm_simt.cuh"
+                             : wide(c)                   ? "gemm_tc2w.cuh"
                              : (c.BM == 256 ? "gemm_tc2.cuh" : "gemm_tc.cuh");
     std::string src;
     try {

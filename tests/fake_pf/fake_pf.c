@@ -97,7 +97,7 @@ int pf_set_host_chunks(pf_ctx *c, int chunks) { return (!c || chunks < 0 || chun
 
 int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
   if (!c || !t) return PF_EINVAL;
-  flog("prepare", c->device);
+  flog(t->BN == 512 ? "prepare_bn512" : "prepare", c->device);
   c->prepared = c->bound = 0;
   if (M <= 0 || N <= 0 || K <= 0) return set_err(c, PF_EINVAL, "M, N, K must be positive");
   if (dt == PF_BF16 || dt == PF_E4M3) {

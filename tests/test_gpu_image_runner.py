@@ -187,6 +187,7 @@ def _tune(args):
     ("bf16", ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "8", "--TN", "8", "--PAD", "1"]),
     ("e4m3", ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "8", "--TN", "8", "--PAD", "1"]),
     ("bf16", ["--BM", "128", "--BN", "256", "--BK", "32", "--TM", "4", "--TN", "16", "--PAD", "0"]),
+    ("bf16", ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "4", "--TN", "16", "--PAD", "2"]),  # 256 x 512
     ("f32", ["--BM", "64", "--BN", "32", "--BK", "16", "--TM", "4", "--TN", "2", "--PAD", "4"]),  # JIT'd tile
 ])
 def test_runner_measure_on_the_real_library(dtype, extra, tmp_path):

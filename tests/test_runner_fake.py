@@ -106,6 +106,17 @@ def test_512_column_pair_tiles(tune_fake, dtype):
     assert rc == 4 and not j["ok"] and "k-atom" in j["error"]
 
 
+@pytest.mark.parametrize("pad,wide", [(0, False), (1, False), (2, True), (4, True), (8, False)])
+def test_search_configs_reach_the_512_column_tiles_through_pad(tune_fake, tmp_path, pad, wide):
+    # the search domain's BN stops at 256: BM=256, BN=256 with PAD=2 or 4 are the 256 x 512 pair tiles
+    log = tmp_path / "calls.log"
+    rc, j, _ = measure(tune_fake, ["--BM", "256", "--BN", "256", "--BK", "32", "--TM", "4", "--TN", "16", "--PAD", str(pad)],
+                       FAKE_PF_LOG=log)
+    assert rc == 0 and j["ok"], j
+    events = log.read_text().split()[::2]
+    assert ("prepare_bn512" in events) == wide and ("prepare" in events) == (not wide)
+
+
 def test_bk_and_pad_are_canonical_on_the_tensor_path(tune_fake):
     rc, j, _ = measure(tune_fake, ["--BM", "128", "--BN", "128", "--BK", "8", "--TM", "4", "--TN", "8", "--PAD", "2"])
     assert rc == 0 and j["ok"]
