@@ -54,7 +54,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--config", default="cfg3_bf16_8192")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--tile", default=None, help="BM,BN,BK,TM,TN,PAD (default: the dtype's best)")
+    ap.add_argument("--tile", default=None,
+                    help="BM,BN,BK,TM,TN,PAD (default: ptxforge_b200.default_tile, the best measured for the shape)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparators", action="store_true")
