@@ -53,7 +53,7 @@ class Attr(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
-# Best-measured defaults per dtype.  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
+# Base tiles per dtype (default_tile() picks by shape from these and WIDE_TILE).  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
 # stage (PAD=1) and as many stages as fit (TM=8 -> 3), raster group 16 M-blocks (TN=16; with the pair kernel's
 # alternating k direction the least DRAM traffic: 0.95 GB per bf16 8192^3 launch vs 1.20 GB at TN=8) -- the lowest energy
 # per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4; 3xTF32: CTA pair,
@@ -329,7 +329,7 @@ def gemm_bias_gelu_noalloc(device: int, dtype: str, tile, M: int, N: int, K: int
     fixed array inside the library).  With sync=True waits for the kernel and returns its status word
     (raising PFError if a bounded device wait ran out); with sync=False returns 0 after queueing."""
     lib = load_library()
-    t = tile if isinstance(tile, Tile) else Tile(*(tile or DEFAULT_TILES[dtype]))
+    t = tile if isinstance(tile, Tile) else Tile(*(tile or default_tile(dtype, M, N, K)))
     s = 0 if stream is None else (stream if isinstance(stream, int) else int(stream.cuda_stream))
     st = ctypes.c_uint(0)
     err = ctypes.create_string_buffer(256)
@@ -339,6 +339,31 @@ def gemm_bias_gelu_noalloc(device: int, dtype: str, tile, M: int, N: int, K: int
     if rc:
         raise PFError(rc, "pf_gemm_bias_gelu_noalloc: " + err.value.decode())
     return st.value
+
+
+def check_operands(A, B, bias, C, dtype: str, require_cuda: bool = True):
+    """(M, N, K) of torch operands for `dtype`, or ValueError: the kernels read and write exactly M x K, K x N,
+    N and M x N elements of the dtype's sizes through TMA, so a tensor of another size or element width would
+    send them past its allocation."""
+    if A.dim() != 2 or B.dim() != 2:
+        raise ValueError(f"A and B must be matrices, got {tuple(A.shape)} and {tuple(B.shape)}")
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K or tuple(bias.shape) != (N,):
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}, bias {tuple(bias.shape)}")
+    if tuple(C.shape) != (M, N):
+        raise ValueError(f"C must be {M} x {N}, got {tuple(C.shape)}")
+    e, o = ELEM_BYTES[dtype], OUT_BYTES[dtype]
+    for name, t, size in (("A", A, e), ("B", B, e), ("bias", bias, 4), ("C", C, o)):
+        if require_cuda and not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous (row-major)")
+        if t.element_size() != size:
+            raise ValueError(f"{name} has {t.element_size()}-byte elements; {dtype} needs {size}")
+    if not bias.is_floating_point():
+        raise ValueError("bias must be float32")
+    return M, N, K
 
 
 _contexts: dict = {}
@@ -364,18 +389,12 @@ def gemm_bias_gelu(A, B, bias, C=None, *, dtype: str | None = None, tile=None, s
 
     if dtype is None:
         dtype = {torch.float32: "f32", torch.bfloat16: "bf16"}.get(A.dtype, "e4m3")
-    M, K = A.shape
-    K2, N = B.shape
-    if K2 != K or bias.shape != (N,):
-        raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}, bias {tuple(bias.shape)}")
-    for t in (A, B, bias):
-        if not t.is_cuda or not t.is_contiguous():
-            raise ValueError("operands must be contiguous CUDA tensors")
-    if bias.dtype != torch.float32:
-        raise ValueError("bias must be float32")
-    out_dtype = torch.float32 if OUT_BYTES[dtype] == 4 else torch.bfloat16
+    if dtype not in DTYPES:
+        raise ValueError(f"unknown dtype {dtype!r} (one of {', '.join(DTYPES)})")
     if C is None:
-        C = torch.empty((M, N), dtype=out_dtype, device=A.device)
+        out_dtype = torch.float32 if OUT_BYTES[dtype] == 4 else torch.bfloat16
+        C = torch.empty((A.shape[0], B.shape[-1]), dtype=out_dtype, device=A.device)
+    M, N, K = check_operands(A, B, bias, C, dtype)
     ctx = context(A.device.index or 0)
     key = (dtype, tuple(tile) if tile else None, M, N, K)
     if getattr(ctx, "_key", None) != key:
