@@ -215,19 +215,25 @@ int pf_shard_rows(int M, int G, int g, int align, int *row0, int *rows);
  * when they call us -- for example a serving process that reserved nearly all of HBM for its own
  * pool at start-up (a cudaMalloc then fails or forces the pool to shrink), or a pipeline that cannot
  * afford the device-wide synchronisation cudaFree implies.  It runs the bf16 / e4m3 tensor-core
- * kernel (the same kernels as pf_launch, chosen by `tile` as in pf_prepare) on caller-owned device
+ * kernel (the kernels of pf_launch, chosen by `tile` as in pf_prepare) on caller-owned device
  * operands without a pf_ctx and without allocating anything: no cudaMalloc, no cudaFree, no host
  * heap.  The kernel's scratch -- its device status word, 4 bytes -- lives in a fixed array of
  * PF_NOALLOC_SCRATCH_BYTES bytes compiled into the library, which every GPU that loads the library
  * keeps until the process exits; a kernel needing more scratch than that is refused (PF_EINVAL).
- *   - The first call on a device looks the array's device address up (once per device, with that
- *     device made current).  Make that first call before any stream capture.
+ *   - Whole tiles only: the stream-K tail, whose partial sums need a workspace, never runs here.  Where
+ *     pf_launch's automatic mode turns that tail on (long multi-wave problems), the two entry points
+ *     round the tail tiles differently (both within the dtype's tolerance); elsewhere they give the
+ *     same bits.
+ *   - The first successful call on a device looks the array's device address up (with that device
+ *     made current) and caches each kernel's launch set-up; a failed look-up is retried by the next
+ *     call.  Make that first call before any stream capture.
  *   - The array is shared by every call on a device and keeps the last call's contents; each call
  *     clears the status word on `stream` before its launch.  Calls that overlap on the GPU (different
  *     streams, no ordering between them) race on it: order them, or use pf_ctx contexts instead.
- *   - `stream` NULL = the CUDA default stream.  With `status_out` NULL the call returns after queueing
- *     the work; with `status_out` non-NULL it synchronises `stream`, stores the status word there and
- *     returns PF_ETIMEOUT if a bounded device wait ran out.
+ *   - `stream` NULL = the CUDA default stream; a stream of another device is refused (PF_EINVAL).
+ *     With `status_out` NULL the call returns after queueing the work; with `status_out` non-NULL it
+ *     synchronises `stream`, stores the status word there and returns PF_ETIMEOUT if a bounded device
+ *     wait ran out.  Each device wait is bounded by 4 s (pf_ctx's default, pf_set_wait_timeout).
  *   - `err` (may be NULL) receives a short message of at most `err_len` bytes on failure.
  * fp32 (PF_F32) is not accepted: its kernel uses no scratch, call pf_launch instead. */
 int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_tile *tile, int M, int N, int K,

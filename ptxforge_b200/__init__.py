@@ -326,9 +326,24 @@ def gemm_bias_gelu_noalloc(device: int, dtype: str, tile, M: int, N: int, K: int
                            scale_a: float = 1.0, scale_b: float = 1.0, stream=None, sync: bool = True) -> int:
     """pf_gemm_bias_gelu_noalloc: the bf16 / e4m3 kernel on caller-owned device operands, for callers
     that cannot allocate GPU memory at call time (no context, no cudaMalloc; the kernel's scratch is a
-    fixed array inside the library).  With sync=True waits for the kernel and returns its status word
-    (raising PFError if a bounded device wait ran out); with sync=False returns 0 after queueing."""
+    fixed array inside the library).  Torch operands are checked as in gemm_bias_gelu (shapes equal to
+    M, N, K, contiguous, element widths of `dtype`, all on `device`; ValueError otherwise), and with no
+    `stream` the call goes on torch's current stream of that device.  With sync=True waits for the kernel
+    and returns its status word (raising PFError if a bounded device wait ran out); with sync=False returns
+    0 after queueing."""
     lib = load_library()
+    if all(hasattr(x, "shape") for x in (A, B, bias, C)):
+        # torch operands: the same checks as gemm_bias_gelu, before anything reaches the TMA maps
+        shape = check_operands(A, B, bias, C, dtype, require_cuda=False)
+        if shape != (M, N, K):
+            raise ValueError(f"operands are {shape[0]} x {shape[1]} x {shape[2]} (M x N x K), "
+                             f"but M, N, K = {M}, {N}, {K}")
+        for name, x in (("A", A), ("B", B), ("bias", bias), ("C", C)):
+            if not x.is_cuda or x.device.index != device:
+                raise ValueError(f"{name} must be a CUDA tensor on device {device}, got {x.device}")
+        if stream is None:  # as gemm_bias_gelu: order after the work torch queued on the current stream
+            import torch
+            stream = torch.cuda.current_stream(A.device)
     t = tile if isinstance(tile, Tile) else Tile(*(tile or default_tile(dtype, M, N, K)))
     s = 0 if stream is None else (stream if isinstance(stream, int) else int(stream.cuda_stream))
     st = ctypes.c_uint(0)

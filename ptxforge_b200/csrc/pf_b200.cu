@@ -327,18 +327,19 @@ const char *cu_err(CUresult r) {
   return s ? s : "unknown CUDA driver error";
 }
 
+// The driver's cuTensorMapEncodeTiled.  A function-local static is initialised exactly once, and threads
+// whose first calls race all wait for that one initialisation (C++11 guarantees it), so none can see a
+// half-initialised value.
 EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  static const EncodeTiledFn fn = [] {
     void *p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -424,20 +425,35 @@ struct DeviceGuard {
   }
 };
 
-int encode_2d(pf_ctx *c, CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+// A 2-D tiled TMA map; on failure a message goes to msg[0..len) (no heap: the no-allocation entry point
+// uses it too).
+int encode_2d_msg(char *msg, size_t len, CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return set_err(c, PF_ECUDA, "cuTensorMapEncodeTiled unavailable from the CUDA driver");
+  if (!enc) {
+    if (msg && len) snprintf(msg, len, "cuTensorMapEncodeTiled unavailable from the CUDA driver");
+    return PF_ECUDA;
+  }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_err(c, PF_ECUDA, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu tensor, box %ux%u", (int)r,
-                   (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+  if (r != CUDA_SUCCESS) {
+    if (msg && len)
+      snprintf(msg, len, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu tensor, box %ux%u", (int)r,
+               (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+    return PF_ECUDA;
+  }
   return PF_OK;
+}
+
+int encode_2d(pf_ctx *c, CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  char msg[200];
+  const int rc = encode_2d_msg(msg, sizeof msg, map, dt, base, inner, outer, row_bytes, box_inner, box_outer, swz);
+  return rc ? set_err(c, rc, "%s", msg) : PF_OK;
 }
 
 // Element types of the tensor path's TMA maps: A and B in the dtype's encoding; C is bf16 except on the
@@ -1223,15 +1239,27 @@ static __device__ __align__(256) unsigned char pf_noalloc_scratch[PF_NOALLOC_SCR
 namespace {
 
 constexpr int kNoallocMaxDevices = 64;
+constexpr int kNoallocMaxKernels = 32;                       // kernel variants whose launch set-up is cached
+constexpr unsigned long long kNoallocWaitNs = 4000000000ull;  // bound of each device wait (pf_ctx's default)
 
-// Per-device set-up, done once with that device current: the array's device address (host code
-// cannot use the symbol itself -- on the host it names a stand-in, not device memory).
+// Per-device set-up, done with that device current: the array's device address (host code cannot use
+// the symbol itself -- on the host it names a stand-in, not device memory), the SM count and compute
+// capability, and per kernel variant its shared-memory attribute and co-resident CTA pairs.  `ready` is set
+// only when the look-ups succeeded, so a failed set-up (for instance a first call made during a stream
+// capture) is tried again by the next call instead of failing every later call.  Fixed-size tables: the
+// entry point allocates nothing, on the host either.
+struct NoallocKernel {
+  const void *func = nullptr;
+  int units = 0;
+};
 struct NoallocDevice {
-  std::once_flag once;
-  cudaError_t setup_err = cudaSuccess;
+  std::mutex mu;
+  bool ready = false;
   unsigned *scratch = nullptr;
   int num_sms = 0;
   int cc_major = 0;
+  NoallocKernel kernels[kNoallocMaxKernels];
+  int n_kernels = 0;
 };
 NoallocDevice g_noalloc_dev[kNoallocMaxDevices];
 
@@ -1243,6 +1271,60 @@ int noalloc_fail(char *err, size_t len, int code, const char *fmt, ...) {
     va_end(ap);
   }
   return code;
+}
+
+// The device's scratch address and properties (first successful call per device does the look-ups).
+cudaError_t noalloc_device_setup(NoallocDevice &d, int device) {
+  std::lock_guard<std::mutex> lk(d.mu);
+  if (d.ready) return cudaSuccess;
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, pf_noalloc_scratch);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
+  d.scratch = static_cast<unsigned *>(p);
+  d.ready = p != nullptr;
+  return d.ready ? cudaSuccess : cudaErrorInvalidSymbol;
+}
+
+// Persistent-grid size for a variant: its co-resident CTAs (1-CTA kernels) or CTA pairs, after raising its
+// dynamic shared-memory limit; cached per (device, variant) once both calls succeeded.
+cudaError_t noalloc_kernel_units(NoallocDevice &d, const Variant &v, int *units) {
+  std::lock_guard<std::mutex> lk(d.mu);
+  for (int i = 0; i < d.n_kernels; ++i)
+    if (d.kernels[i].func == v.func) {
+      *units = d.kernels[i].units;
+      return cudaSuccess;
+    }
+  cudaError_t ce = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
+  if (ce != cudaSuccess) return ce;
+  int u = d.num_sms;
+  if (v.cta_per_tile == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (d.num_sms / 2));
+    cfg.blockDim = dim3(v.threads);
+    cfg.dynamicSmemBytes = v.smem;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, v.func, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      *units = d.num_sms / 2;  // not cached: the next call asks again
+      return cudaSuccess;
+    }
+    u = clusters;
+  }
+  if (d.n_kernels < kNoallocMaxKernels) d.kernels[d.n_kernels++] = {v.func, u};
+  *units = u;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -1266,19 +1348,20 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   }
   DeviceGuard g(device);
   NoallocDevice &d = g_noalloc_dev[device];
-  std::call_once(d.once, [&] {
-    void *p = nullptr;
-    d.setup_err = cudaGetSymbolAddress(&p, pf_noalloc_scratch);
-    if (d.setup_err == cudaSuccess)
-      d.setup_err = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
-    if (d.setup_err == cudaSuccess)
-      d.setup_err = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, device);
-    d.scratch = static_cast<unsigned *>(p);
-  });
-  if (d.setup_err != cudaSuccess || !d.scratch)
+  cudaError_t ce = noalloc_device_setup(d, device);
+  if (ce != cudaSuccess)
     return noalloc_fail(err, err_len, PF_ECUDA, "scratch set-up on device %d failed: %s", device,
-                        cudaGetErrorString(d.setup_err));
+                        cudaGetErrorString(ce));
   if (d.cc_major != 10) return noalloc_fail(err, err_len, PF_ENODEV, "device %d is not an sm_100 GPU", device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int stream_dev = -1;
+  ce = cudaStreamGetDevice(s, &stream_dev);
+  if (ce != cudaSuccess) {
+    cudaGetLastError();
+    return noalloc_fail(err, err_len, PF_EINVAL, "stream is not a valid CUDA stream: %s", cudaGetErrorString(ce));
+  }
+  if (stream_dev != device)
+    return noalloc_fail(err, err_len, PF_EINVAL, "stream belongs to device %d, not device %d", stream_dev, device);
 
   // Kernel variant and layout rules: those of pf_prepare / pf_bind.
   if ((t->BM != 128 && t->BM != 256) || t->BK != 32 || (t->PAD != 0 && t->PAD != 1) || t->TN < 1 || t->TN > 64)
@@ -1293,46 +1376,35 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
     return noalloc_fail(err, err_len, PF_ESHAPE, "rows of A, B and C must be multiples of 16 bytes (N=%d, K=%d)", N, K);
   if (!aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(bias))
     return noalloc_fail(err, err_len, PF_EINVAL, "operands must be 16-byte aligned");
-  // Scratch this kernel needs: one 32-bit status word.
+  // Scratch this kernel needs: one 32-bit status word.  Whole tiles only: the stream-K tail, which needs a
+  // workspace of partial sums, is never used here.
   constexpr size_t kScratchNeeded = sizeof(unsigned);
   if (kScratchNeeded > sizeof(pf_noalloc_scratch))
     return noalloc_fail(err, err_len, PF_EINVAL, "the kernel needs %zu bytes of scratch; the fixed area holds %zu",
                         kScratchNeeded, sizeof(pf_noalloc_scratch));
 
-  cudaError_t ce = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
-  if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce));
-  int units = d.num_sms;
-  if (v.cta_per_tile == 2) {
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * (d.num_sms / 2));
-    cfg.blockDim = dim3(v.threads);
-    cfg.dynamicSmemBytes = v.smem;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, v.func, &cfg) != cudaSuccess || clusters <= 0) {
-      cudaGetLastError();
-      clusters = d.num_sms / 2;
-    }
-    units = clusters;
+  int units = 0;
+  ce = noalloc_kernel_units(d, v, &units);
+  if (ce != cudaSuccess) {
+    cudaGetLastError();
+    return noalloc_fail(err, err_len, PF_ECUDA, "kernel set-up: %s", cudaGetErrorString(ce));
   }
 
   const CUtensorMapDataType in_t =
       dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUtensorMap tmA, tmB, tmC, tmCt;
-  if (encode_2d(nullptr, &tmA, in_t, A, K, M, K * e, v.a_box_k, v.a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      encode_2d(nullptr, &tmB, in_t, B, N, K, N * e, v.b_chunk_n, v.bk_elems, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      encode_2d(nullptr, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
-    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");
+  char msg[200];
+  if (encode_2d_msg(msg, sizeof msg, &tmA, in_t, A, K, M, K * e, v.a_box_k, v.a_box_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      encode_2d_msg(msg, sizeof msg, &tmB, in_t, B, N, K, N * e, v.b_chunk_n, v.bk_elems,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      encode_2d_msg(msg, sizeof msg, &tmC, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 64, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding: %s", msg);
   tmCt = tmC;
-  if (v.bn % 64 != 0 &&
-      encode_2d(nullptr, &tmCt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
-    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding failed");
+  if (v.bn % 64 != 0 && encode_2d_msg(msg, sizeof msg, &tmCt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, N * 2ull,
+                                      32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    return noalloc_fail(err, err_len, PF_ECUDA, "TMA tensor-map encoding: %s", msg);
 
   TcParams p;
   p.bias = bias;
@@ -1346,9 +1418,8 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   p.k_blocks = (K + v.bk_elems - 1) / v.bk_elems;
   p.group_m = std::max(1, std::min(t->TN, p.num_m_blocks));
   p.status = d.scratch;  // word 0 of the fixed scratch area
-  p.timeout_ns = 4000000000ull;
+  p.timeout_ns = kNoallocWaitNs;
 
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   ce = cudaMemsetAsync(d.scratch, 0, sizeof(unsigned), s);  // the last call's status must not leak in
   if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
   v.launch_tc(dim3(std::min(p.num_tiles, units) * v.cta_per_tile), s, tmA, tmB, tmC, tmCt, p);

@@ -45,3 +45,19 @@ def test_host_tensors_are_refused_before_any_launch():
         pf.gemm_bias_gelu(*ops()[:3], dtype="bf16")
     with pytest.raises(ValueError, match="unknown dtype"):
         pf.gemm_bias_gelu(*ops()[:3], dtype="fp16")
+
+
+def test_noalloc_checks_torch_operands_before_the_c_abi():
+    """pf_gemm_bias_gelu_noalloc's Python view refuses what gemm_bias_gelu refuses, and more: its M, N, K
+    arguments must equal the operands' shapes and every operand must sit on `device` -- before the C ABI,
+    which would hand the pointers to TMA maps of the stated sizes."""
+    A, B, bias, C = ops()
+    tile = (128, 256, 32, 4, 16, 0)
+    with pytest.raises(ValueError, match="C must be 64 x 32"):
+        pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 64, 32, 48, A, B, bias, torch.zeros(32, 32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="A has 4-byte"):
+        pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 64, 32, 48, A.float(), B, bias, C)
+    with pytest.raises(ValueError, match="but M, N, K = 128, 32, 48"):
+        pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 128, 32, 48, A, B, bias, C)
+    with pytest.raises(ValueError, match="CUDA tensor on device 0"):
+        pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 64, 32, 48, A, B, bias, C)

@@ -7,9 +7,12 @@ cudaFree brings.  For them the tensor-core kernel also runs without a context: i
 device status word, sits in a fixed array compiled into the library.
 
 Checked: two calls in a row produce the same C as the context-based entry point (pf_prepare / pf_bind /
-pf_launch) -- within the tolerance the parity tests use, and in fact bit for bit; the calls leave the
-device's free memory unchanged; requests it cannot serve are refused with a message.  The file name makes
-pytest collect it last, so a failure here comes after every other test has run; it also passes alone.
+pf_launch) -- within the tolerance the parity tests use, and bit for bit on these shapes, where both run
+whole tiles (pf_launch's automatic stream-K tail starts at three waves of tiles; the no-allocation call
+never runs it) -- and each is also within tolerance of the oracle's fp64 result on the same inputs; the
+calls leave the device's free memory unchanged; requests it cannot serve are refused with a message.  The
+file name makes pytest collect it last, so a failure here comes after every other test has run; it also
+passes alone.
 """
 import numpy as np
 import pytest
@@ -49,11 +52,12 @@ CASES = [("cfg3_bf16_8192", (128, 256, 32, 4, 16, 0), (512, 768, 640)),
 
 
 @pytest.mark.parametrize("name,tile,shape", CASES)
-def test_two_calls_match_the_context_entry_point(pf, ctx, name, tile, shape):
+def test_two_calls_match_the_context_entry_point(pf, ctx, oracle_mod, name, tile, shape):
     w = wl.scaled(wl.CONFIGS[name], *shape)
     inp = wl.make_inputs(w, seed=21)
     A, B, bias = _operands(w, inp)
     stream = torch.cuda.current_stream()
+    ref64 = oracle_mod.full_f64(inp.A, inp.B, inp.bias, inp.scale_a * inp.scale_b)
 
     C_ref = _nan_c(w)
     ctx.prepare(w.dtype, tile, w.M, w.N, w.K)
@@ -69,6 +73,7 @@ def test_two_calls_match_the_context_entry_point(pf, ctx, name, tile, shape):
         assert status == 0
         assert not torch.isnan(C.float()).any()
         assert _max_rel_err(C_ref.float(), C.float()) <= TOL[w.dtype]
+        assert oracle_mod.max_rel_err(ref64, C.float().cpu().numpy()) <= TOL[w.dtype]
         assert torch.equal(C, C_ref)
 
 
