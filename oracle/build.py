@@ -24,7 +24,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-REF_ROOT = os.environ.get("PTXFORGE_REFERENCE", "/root/reference")
+# The reference source tree: $PTXFORGE_REFERENCE, else a `reference` directory beside the repository; where
+# neither exists the reference builds are skipped (the prebuilt files in _ref/, if any, stay in use).
+REF_ROOT = os.environ.get("PTXFORGE_REFERENCE") or os.path.normpath(os.path.join(ROOT, os.pardir, "reference"))
 REF_DIR = os.path.join(HERE, "_ref")
 LIB = os.path.join(HERE, "liboracle.so")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")

@@ -69,7 +69,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
-REF_ROOT = os.environ.get("PTXFORGE_REFERENCE", "/root/reference")
+# The PTXForge source tree the runner plugs into: $PTXFORGE_REFERENCE, else a `reference` directory beside the
+# repository.  Where neither exists the tuner CLI is not built (build_tune returns None).
+REF_ROOT = os.environ.get("PTXFORGE_REFERENCE") or os.path.normpath(os.path.join(ROOT, os.pardir, "reference"))
 TUNE_SRC = os.path.join(HERE, "host", "tune_b200.cpp")
 TUNE_BIN = os.path.join(ROOT, "build", "ptxforge-tune-b200")
 

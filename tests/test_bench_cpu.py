@@ -33,6 +33,13 @@ def test_reference_arm_prints_the_contract_line():
     assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
     assert d["cpu_baseline"]["kind"] == "port" and "rows" in d["cpu_baseline"]["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # ms_per_step is the measured time of one step's row sample (steps x ms_per_step is the timed region), and
+    # the sample is named in config
+    rows = d["config"]["rows_sampled"]
+    assert 1 <= rows <= 512 and d["ms_per_step"] > 0
+    assert abs(d["value"] - 2.0 * rows * 512 * 512 / (d["ms_per_step"] * 1e-3) / 1e12) <= 0.02 * d["value"]
+    one = d["cpu_baseline"]["single_thread"]
+    assert one["cores"] == 1 and one["value"] > 0 and one["unit"] == "TFLOP/s"
 
 
 def test_reference_arm_other_ranks_print_nothing():
@@ -47,3 +54,16 @@ def test_l2_note():
     from ptxforge_b200 import workloads as wl
     assert "exceed the 126 MB L2" in bench.l2_note(wl.CONFIGS["cfg3_bf16_8192"])
     assert "fit in the 126 MB L2" in bench.l2_note(wl.CONFIGS["cfg1_f32_512"])
+
+
+def test_energy_and_clocks_print_null_with_a_reason():
+    import bench
+    c = bench.ClockSampler.__new__(bench.ClockSampler)
+    c.ok, c.samples, c.reasons, c.power, c.max_mhz = True, [], set(), [], 1965
+    c.e0 = c.e1 = 1000
+    e = c.energy(20)
+    assert e["mj_per_step"] is None and "did not advance" in e["reason"]
+    s = c.summary()
+    assert s["sm_mhz"] is None and s["samples"] == 0 and "no sample" in s["reason"]
+    c.e1 = 3000
+    assert c.energy(20)["mj_per_step"] == 100.0
