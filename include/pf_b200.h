@@ -149,12 +149,19 @@ int pf_attrs(pf_ctx *ctx, pf_attr *out);
  * bit 2: epilogue wait, bit 3: teardown wait, bit 4: 3xTF32 split wait). */
 int pf_device_status(pf_ctx *ctx, unsigned *err_word);
 
-/* Stream-K tail of the CTA-pair (BM=256) kernels: -1 auto (default: with at least 3 waves of tiles when the
- * last partial wave would waste more than 3 % of the launch; PF_F32_3XTF32 also below that when whole tiles
- * would leave a quarter of the CTA pairs idle, given 4 leftover k-blocks per pair), 0 off (every tile whole:
- * results independent of the launch shape, bit for bit), 1 on whenever there is a partial wave.  With the tail, the leftover tiles'
- * k-iterations are spread over all resident CTA pairs and their fp32 partial sums added in a fixed
- * order (deterministic for a given shape); the context keeps a workspace of 256 KB per CTA pair. */
+/* Stream-K of the CTA-pair (BM=256) kernels: -1 auto (default), 0 off (every tile whole: results
+ * independent of the launch shape, bit for bit), 1 on wherever the kernel can.
+ *   - 256 x 256 pair tiles (and PF_F32_3XTF32): a stream-K tail -- the leftover tiles' k-iterations of a
+ *     partial last wave are spread over all resident CTA pairs.  Auto: with at least 3 waves of tiles when the
+ *     last partial wave would waste more than 3 % of the launch; PF_F32_3XTF32 also below that when whole tiles
+ *     would leave a quarter of the CTA pairs idle, given 4 leftover k-blocks per pair.  1: whenever there is a
+ *     partial wave.  Workspace: 256 KB per CTA pair.
+ *   - 256 x 512 pair tiles: row-band stream-K -- each row block of tiles is shared by P = pairs / row blocks
+ *     pairs, each taking an equal contiguous share of its k-iterations.  Auto: off (measured slower on the
+ *     row shards it would serve: every extra unit boundary stalls the kernel's single accumulator); 1:
+ *     wherever P >= 2.  Workspace: 512 KB per CTA pair.
+ * Split tiles' fp32 partial sums are added in a fixed order (deterministic for a given shape), but in a
+ * different rounding from whole tiles. */
 int pf_set_stream_k(pf_ctx *ctx, int mode);
 
 /* Row chunks of the host-buffer pipelines (pf_run_host, pf_run_host_rows): 0 = default (8), else at most

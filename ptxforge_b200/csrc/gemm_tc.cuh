@@ -54,6 +54,11 @@ struct TcParams {
   int dir_num_m_blocks = 0;   // row blocks of the whole problem
   int dir_group_m = 0;        // raster group of the whole problem's launch
   int dir_workers = 0;        // workers (CTAs or CTA pairs) of the whole problem's launch
+  // Row-band stream-K (256 x 512 pair kernel only; 0 = off): each row block of tiles is a band worked by this
+  // many pairs, each taking an equal contiguous share of the band's k-iterations (tiles left to right, k
+  // ascending).  Pairs at the same position in different bands read the same B panel at the same time.
+  // Partials go to sk_partials as [workers][2 CTAs][128 x 512] fp32; flags and epoch as above.
+  int sk_band_workers = 0;
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).

@@ -7,7 +7,7 @@
 //
 // Each CTA's 128 accumulator rows x 512 fp32 columns fill its TMEM, so there is one accumulator per CTA,
 // handed back in two halves: the epilogue drains columns [0, 256) and releases them, and the next
-// tile's MMAs into that half start while it drains [256, 512).  The MMA issuer runs a stage's second-half
+// unit's MMAs into that half start while it drains [256, 512).  The MMA issuer runs a stage's second-half
 // MMAs as soon as that half is free; until then it holds at most STAGES stages whose second half is
 // still to do (their shared memory stays loaded), and waits only when all of them are held.
 //   * TMA (both CTAs): per stage, A rows [m0 + 128*rank, +128) and, for each half h, B columns
@@ -18,7 +18,18 @@
 //     each half released to the leader's `tempty[h]` right after its last TMEM load.  With 8 warps two
 //     share each 32-lane quarter of TMEM and split a half's 256 columns, so a half drains in about half the
 //     time: the tensor pipe waits on that drain at every tile boundary.
-// Whole tiles only (no stream-K tail); the k direction alternates by wave as in the other kernels.
+//
+// Work units.  Whole tiles round-robin over the pairs (k direction alternating by wave as in the other
+// kernels), or -- when p.sk_band_workers > 0 -- row-band stream-K: each row block of tiles is a band
+// shared by P pairs, pair j of a band taking k-iterations [j*S/P, (j+1)*S/P) of the band's S = tiles x k
+// blocks (tiles left to right, k ascending).  A row shard of 1,024 x 8,192 has 64 tiles for 74 pairs:
+// whole tiles leave 10 pairs idle, 4 bands of 18 pairs keep 72 busy.  Bands rather than one stream over all
+// tiles because pairs j of every band then work on the same B panel at the same k at the same time, so each
+// B slab comes from DRAM once and from L2 for the other bands; a stream-K order that does not line the tiles
+// of a B panel up in time re-reads B from DRAM per row block.  A tile split between pairs is finished by the
+// pair holding its first k-block (the "head", always a pair's last unit); the others ("partials", always a
+// pair's first unit) write their fp32 sums to a workspace and raise a flag tagged with the launch's epoch;
+// the head adds them before its epilogue.  Every wait is bounded.
 #pragma once
 
 #include "gemm_tc2.cuh"
@@ -50,8 +61,9 @@ struct Tc2wConfig {
   static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
   static constexpr int EPI_BUFS = 2;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1;
+  static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1 + 1;
   static constexpr int TMEM_COLS = 512;                      // one accumulator: two halves of 256 columns
+  static constexpr int PARTIAL_FLOATS = BM_CTA * BN;         // one CTA's share of a tile, fp32
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
   static constexpr uint32_t IDESC =
@@ -60,6 +72,50 @@ struct Tc2wConfig {
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
   static_assert(B_CHUNKS_HALF >= 1, "each CTA supplies at least one 128-byte box of B per half");
 };
+
+// One unit of a pair's work: tile (mb, nb), k-blocks [kb0, kb1), whole / head / partial (kUnit*).
+struct WideUnit {
+  int mb, nb, kb0, kb1, kind;
+  bool reversed;  // whole tiles of odd waves walk k downwards (data-parallel schedule only)
+};
+
+// First k-iteration of band position j (of P) in a band of S k-iterations, floor(j * S / P), in 32-bit
+// arithmetic (S = q * P + r: j * q + j * r / P; the host keeps S below 2^31 in band mode).
+__device__ __forceinline__ int band_start(int j, int P, int S) { return j * (S / P) + (j * (S % P)) / P; }
+
+// Unit `u` of pair `w` of `W`; false past the pair's last unit.
+__device__ __forceinline__ bool wide_unit(int w, int W, int u, const TcParams &p, WideUnit &out) {
+  if (p.sk_band_workers <= 0) {
+    const int t = w + u * W;
+    if (t >= p.num_tiles) return false;
+    int mb, nb;
+    tile_coords(t, p, mb, nb);
+    out = {mb, nb, 0, p.k_blocks, kUnitWhole, tile_k_reversed(p, mb, nb, W)};
+    return true;
+  }
+  const int P = p.sk_band_workers;
+  const int g = w / P, j = w % P;
+  if (g >= p.num_m_blocks) return false;
+  const int KB = p.k_blocks;
+  const int S = p.num_n_blocks * KB;
+  const int e = band_start(j + 1, P, S);
+  int pos = band_start(j, P, S);
+  for (int i = 0; pos < e; ++i) {
+    const int nb = pos / KB;
+    const int seg_end = min(e, (nb + 1) * KB);
+    if (i == u) {
+      out.mb = g;
+      out.nb = nb;
+      out.kb0 = pos - nb * KB;
+      out.kb1 = seg_end - nb * KB;
+      out.kind = out.kb0 == 0 ? (out.kb1 == KB ? kUnitWhole : kUnitHead) : kUnitPartial;
+      out.reversed = false;
+      return true;
+    }
+    pos = seg_end;
+  }
+  return false;
+}
 
 // One epilogue warp's 32 rows x 128 columns of one accumulator half: the four 32-column TMEM loads first,
 // then the half is handed back (`release`) before any epilogue math, which runs from registers while the
@@ -103,6 +159,33 @@ __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, i
   }
 }
 
+// A split tile's fp32 partial sums: one epilogue warp's 32 rows x COLS columns of a half, from TMEM to its
+// slot (float4 index ((col / 4) * 32 + lane) from `dst`: each warp-wide store covers 512 contiguous bytes).
+// 64 columns at a time are loaded, then stored; the half is released after its last load.
+template <int COLS, class Release>
+__device__ __forceinline__ void partial_rows(uint32_t t_col, float4 *dst, int lane, Release release) {
+  static_assert(COLS % 64 == 0, "64-column steps");
+#pragma unroll 1
+  for (int s = 0; s < COLS / 64; ++s) {
+    uint32_t v[2][32];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) tmem_ld_32x32b_x32(t_col + s * 64 + c * 32, v[c]);
+    tmem_ld_wait();
+    if (s == COLS / 64 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      release();
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4)
+        __stcg(dst + ((s * 64 + c * 32) / 4 + j4) * 32 + lane,
+               make_float4(__uint_as_float(v[c][j4 * 4 + 0]), __uint_as_float(v[c][j4 * 4 + 1]),
+                           __uint_as_float(v[c][j4 * 4 + 2]), __uint_as_float(v[c][j4 * 4 + 3])));
+  }
+}
+
 template <class Cfg>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     gemm_bias_gelu_tc2w(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -120,7 +203,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [1] both: accumulator ready
   uint64_t *tempty = tfull + 1;                 // [2] leader: both CTAs drained half h
   uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *epi_sync = drain + 1;               // [1] the epilogue warps wrote this pair's partial
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_sync + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -141,6 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     mbar_init(&tempty[0], 2 * Cfg::EPI_WARPS);
     mbar_init(&tempty[1], 2 * Cfg::EPI_WARPS);
     mbar_init(drain, 1);
+    mbar_init(epi_sync, Cfg::EPI_WARPS);        // completes at most once: a pair has at most one partial
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -167,14 +252,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int issued = 0;
-      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
-        int mb, nb;
-        tile_coords(t, p, mb, nb);
-        const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
-        const int n0 = nb * Cfg::BN + static_cast<int>(rank) * (Cfg::HALF_N / 2);
-        const bool reversed = tile_k_reversed(p, mb, nb, num_pairs);
-        for (int i = 0; i < p.k_blocks; ++i) {
-          const int kb = reversed ? p.k_blocks - 1 - i : i;
+      WideUnit un;
+      for (int u = 0; ok && wide_unit(pair, num_pairs, u, p, un); ++u) {
+        const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
+        const int n0 = un.nb * Cfg::BN + static_cast<int>(rank) * (Cfg::HALF_N / 2);
+        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
+          const int kb = un.reversed ? un.kb1 - 1 - i : un.kb0 + i;
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
@@ -211,10 +294,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t tphase = 0;  // parity of this pair's tile count: the halves are released once per tile
+      uint32_t tphase = 0;  // parity of this pair's unit count: the halves are released once per unit
       bool ok = true;
       const uint32_t tempty1_addr = smem_u32(&tempty[1]);
-      // Half h's MMAs of the stage in ring slot s, the tile's i-th k step.
+      // Half h's MMAs of the stage in ring slot s, the unit's i-th k step.
       auto issue_half = [&](int s, int h, int i) {
         const uint32_t a_addr = smem_u32(sA + s * Cfg::A_BYTES);
         const uint32_t b_addr = smem_u32(sB + s * Cfg::B_BYTES + h * Cfg::B_HALF_BYTES);
@@ -239,8 +322,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           tc_commit_pair_mc(&empty[s], 0x3);
         }
       };
-      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
-        // The first half of the accumulator must be drained of the previous tile.
+      WideUnit un;
+      for (int u = 0; ok && wide_unit(pair, num_pairs, u, p, un); ++u) {
+        const int steps = un.kb1 - un.kb0;
+        // The first half of the accumulator must be drained of the previous unit.
         if (!mbar_wait_cluster(&tempty[0], tphase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
           ok = false;
@@ -250,7 +335,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         bool second_free = false;
         int pending = 0;  // stages whose second-half MMAs wait for the second half of TMEM
         int last = 0;
-        for (int i = 0; i < p.k_blocks; ++i) {
+        for (int i = 0; i < steps; ++i) {
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
@@ -285,14 +370,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         if (!ok) break;
         if (pending > 0) {
-          // A tile of fewer k steps than stages: its second half waits here.
+          // A unit of fewer k steps than stages: its second half waits here.
           if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
             break;
           }
           tc_fence_after();
-          flush(pending, last, p.k_blocks - 1);
+          flush(pending, last, steps - 1);
         }
         tc_commit_pair_mc(tfull, 0x3);
         tphase ^= 1u;
@@ -311,16 +396,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     int buf = 0;
     const uint32_t tempty0_leader = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t tempty1_leader = mapa_shared(smem_u32(&tempty[1]), 0);
-    for (int t = pair; t < p.num_tiles; t += num_pairs) {
-      int mb, nb;
-      tile_coords(t, p, mb, nb);
+    // This warp's share of pair w's partial slot: its 32 rows (TMEM quarter q) of this CTA's 128, stored
+    // columns-of-4 major so a warp-wide 16-byte access covers 512 contiguous bytes.
+    auto slot = [&](int w) -> float4 * {
+      return reinterpret_cast<float4 *>(p.sk_partials +
+                                        (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
+                                        static_cast<size_t>(q) * 32 * Cfg::BN);
+    };
+    WideUnit un;
+    for (int u = 0; wide_unit(pair, num_pairs, u, p, un); ++u) {
       const bool waited = mbar_wait(tfull, tphase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
         break;
       }
       tc_fence_after();
-      const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
+      const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
+      const int n_tile = un.nb * Cfg::BN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
       auto release0 = [&] {
         if (lane == 0) mbar_arrive_cluster(tempty0_leader);
@@ -328,16 +420,97 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       auto release1 = [&] {
         if (lane == 0) mbar_arrive_cluster(tempty1_leader);
       };
-      if constexpr (Cfg::EPI_COLS_WARP == 128) {
-        // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
-        epilogue_rows128_early(t_row + col0, m0, nb * Cfg::BN + col0, p, &tmC, ebuf, buf, lane, release0);
-        epilogue_rows128_early(t_row + Cfg::HALF_N + col0, m0, nb * Cfg::BN + Cfg::HALF_N + col0, p, &tmC, ebuf, buf,
-                               lane, release1);
-      } else {
-        epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, nb * Cfg::BN + col0, p, &tmC, nullptr, ebuf, buf, lane,
-                                          release0);
-        epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, m0, nb * Cfg::BN + Cfg::HALF_N + col0, p, &tmC,
-                                          nullptr, ebuf, buf, lane, release1);
+      if (un.kind == kUnitPartial) {
+        // This pair's first k-blocks of a tile another pair finishes: fp32 sums to the workspace, then the flag.
+        float4 *dst = slot(pair);
+        partial_rows<Cfg::EPI_COLS_WARP>(t_row + col0, dst + (col0 / 4) * 32, lane, release0);
+        partial_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, dst + ((Cfg::HALF_N + col0) / 4) * 32, lane,
+                                         release1);
+        // Every warp's stores are visible device-wide before it arrives; one lane publishes the flag once
+        // all of them have (a bounded wait, never a hardware barrier a departed warp could block).
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_sync);
+        if (ew == 0 && lane == 0) {
+          if (mbar_wait(epi_sync, 0, p.timeout_ns, abort_flag))
+            st_release_gpu(p.sk_flags + pair * 2 + rank, p.epoch);
+          else
+            fail(kErrEpilogueWait);
+        }
+      } else if (un.kind == kUnitHead) {
+        // The first k-blocks of a tile whose later k-blocks the next pairs of this band summed: wait for their
+        // flags (bounded), then fold their partials into the accumulator.  They are the band positions j' > j
+        // whose share starts inside this tile: floor(j' S / P) < tile_end, i.e. j' < tile_end P / S (the host
+        // keeps S * P below 2^31).
+        const int P = p.sk_band_workers;
+        const int j = pair % P;
+        const int S = p.num_n_blocks * p.k_blocks;
+        const int tile_end = (un.nb + 1) * p.k_blocks;
+        const int last = pair + min(P - 1, (tile_end * P + S - 1) / S - 1) - j;
+        bool ok = true;
+        if (lane == 0) {
+          for (int w = pair + 1; w <= last && ok; ++w) {
+            const unsigned *flag = p.sk_flags + w * 2 + rank;
+            if (ld_acquire_gpu(flag) != p.epoch) {
+              const uint64_t t0 = globaltimer_ns();
+              while (ld_acquire_gpu(flag) != p.epoch) {
+                if (*abort_flag || globaltimer_ns() - t0 > p.timeout_ns) {
+                  ok = false;
+                  break;
+                }
+                __nanosleep(256);
+              }
+            }
+          }
+          if (!ok) fail(kErrEpilogueWait);
+        }
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        for (int w = pair + 1; w <= last; ++w) (void)ld_acquire_gpu(p.sk_flags + w * 2 + rank);  // every lane
+        // Fold the partials of pairs [pair + 1, last] into this warp's accumulator rows in TMEM, 64 columns at a
+        // time: both 32-column TMEM loads and all 16 partial loads of the first contributor in flight together,
+        // add, store back; the tile then drains through the whole-tile epilogue below.
+        const float4 *first_slot = slot(pair + 1) + lane;
+        const int n_contrib = last - pair;
+#pragma unroll 1
+        for (int c = 0; c < 2 * Cfg::EPI_COLS_WARP / 64; ++c) {
+          const int col = (c / (Cfg::EPI_COLS_WARP / 64)) * Cfg::HALF_N + col0 + (c % (Cfg::EPI_COLS_WARP / 64)) * 64;
+          uint32_t v[2][32];
+          tmem_ld_32x32b_x32(t_row + col, v[0]);
+          tmem_ld_32x32b_x32(t_row + col + 32, v[1]);
+          const float4 *src = first_slot + (col / 4) * 32;
+#pragma unroll 1
+          for (int w = 0; w < n_contrib; ++w, src += 2 * Cfg::PARTIAL_FLOATS / 4) {
+            float4 s4[16];
+#pragma unroll
+            for (int j4 = 0; j4 < 16; ++j4) s4[j4] = __ldcg(src + j4 * 32);
+            if (w == 0) tmem_ld_wait();
+#pragma unroll
+            for (int j4 = 0; j4 < 16; ++j4) {
+              uint32_t *d = &v[j4 / 8][(j4 % 8) * 4];
+              d[0] = __float_as_uint(__uint_as_float(d[0]) + s4[j4].x);
+              d[1] = __float_as_uint(__uint_as_float(d[1]) + s4[j4].y);
+              d[2] = __float_as_uint(__uint_as_float(d[2]) + s4[j4].z);
+              d[3] = __float_as_uint(__uint_as_float(d[3]) + s4[j4].w);
+            }
+          }
+          if (n_contrib <= 0) tmem_ld_wait();
+          tmem_st_32x32b_x32(t_row + col, v[0]);
+          tmem_st_32x32b_x32(t_row + col + 32, v[1]);
+        }
+        tmem_st_wait();  // the folded sums are in TMEM before the epilogue below reads them back
+      }
+      if (un.kind != kUnitPartial) {
+        if constexpr (Cfg::EPI_COLS_WARP == 128) {
+          // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
+          epilogue_rows128_early(t_row + col0, m0, n_tile + col0, p, &tmC, ebuf, buf, lane, release0);
+          epilogue_rows128_early(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC, ebuf, buf,
+                                 lane, release1);
+        } else {
+          epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, n_tile + col0, p, &tmC, nullptr, ebuf, buf, lane,
+                                            release0);
+          epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
+                                            nullptr, ebuf, buf, lane, release1);
+        }
       }
       tphase ^= 1u;
     }

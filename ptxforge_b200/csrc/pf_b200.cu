@@ -59,6 +59,8 @@ struct Variant {
   double sk_min_waves = 3.0;
   double sk_low_util = 0.0;
   int sk_min_share = 1;
+  bool sk_band = false;         // the kernel can run row-band stream-K (p.sk_band_workers)
+  int partial_cols = 256;       // fp32 columns of one CTA's stream-K partial (x 128 rows)
   int b_chunk_n = 0;
   // (grid, stream, A map, B map, C map, C tail map -- used by tiles whose width is not a multiple of 64)
   void (*launch_tc)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
@@ -158,6 +160,8 @@ Variant make_tc2w_variant() {
   v.a_box_k = Cfg::ATOM_K;
   v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 2;
+  v.sk_band = true;
+  v.partial_cols = Cfg::BN;
   v.launch_tc = &launch_tc2w_impl<DT, ST, EW>;
   return v;
 }
@@ -244,6 +248,17 @@ const SimtEntry kSimtTable[] = {
     {{32, 32, 32, 4, 2, 2}, &make_simt_variant<32, 32, 32, 4, 2, 2>},
     {{64, 32, 32, 4, 2, 2}, &make_simt_variant<64, 32, 32, 4, 2, 2>},
     {{32, 64, 32, 4, 2, 2}, &make_simt_variant<32, 64, 32, 4, 2, 2>},
+    // 64-thread CTAs with 8 x 8 micro-tiles: eight share an SM at 128 registers, so small block tiles fill
+    // the SMs evenly (2048^2 outputs: 1,024 tiles of 64 x 64 for 148 x 8 slots)
+    {{64, 64, 8, 8, 8, 4}, &make_simt_variant<64, 64, 8, 8, 8, 4>},
+    {{64, 64, 16, 8, 8, 4}, &make_simt_variant<64, 64, 16, 8, 8, 4>},
+    {{128, 64, 8, 8, 8, 4}, &make_simt_variant<128, 64, 8, 8, 8, 4>},
+    {{64, 128, 8, 8, 8, 4}, &make_simt_variant<64, 128, 8, 8, 8, 4>},
+    {{64, 32, 8, 8, 4, 4}, &make_simt_variant<64, 32, 8, 8, 4, 4>},
+    {{32, 64, 8, 4, 8, 4}, &make_simt_variant<32, 64, 8, 4, 8, 4>},
+    {{32, 32, 8, 4, 4, 4}, &make_simt_variant<32, 32, 8, 4, 4, 4>},
+    {{32, 32, 16, 4, 4, 4}, &make_simt_variant<32, 32, 16, 4, 4, 4>},
+    {{32, 32, 32, 4, 4, 4}, &make_simt_variant<32, 32, 32, 4, 4, 4>},
 };
 
 bool same_tile(const pf_tile &a, const pf_tile &b) {
@@ -522,8 +537,29 @@ int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
   return R;
 }
 
+// Pairs per band of a row-band stream-K launch of the 256 x 512 pair kernel (0 = whole tiles).  Each of the
+// launch's row blocks gets P = W / (row blocks) pairs, which share its k-iterations evenly, so the busiest pair
+// does ceil(S / P) k-blocks of the band's S instead of ceil(tiles / W) whole tiles' worth: on the 8- and 4-GPU
+// row shards of 8192^3 (4 and 8 bands of 18 and 9 pairs) 114 / 228 k-blocks per pair instead of 128 / 256.
+// Measured on B200 (CUDA events, bursts of 20 launches) it does not pay: 1,024 rows 99.7 -> 105.1 us, 2,048
+// rows 188.7 -> 190.9 us.  ncu of one launch each: the busy SMs' tensor pipes fall from 78.9 to 68.1 % of
+// cycles -- each pair runs two units instead of one, and with one 512-column accumulator per CTA every unit
+// boundary (and the partial's 256 KB drain per CTA, and the head's fold) stalls the MMAs for a few thousand
+// cycles, more than the 14 / 28 k-blocks saved.  So auto mode keeps whole tiles; 1 (pf_set_stream_k) runs it
+// wherever P >= 2 (tested against the oracle and against whole tiles).
+int band_workers(const pf_ctx *c, int num_m_blocks, int num_n_blocks, int k_blocks) {
+  if (!c->var.sk_band || c->stream_k <= 0) return 0;
+  const int W = c->max_units;
+  const int P = W / num_m_blocks;
+  if (P < 2) return 0;
+  // the kernel's band arithmetic is 32-bit: S * P < 2^31
+  const long long S = static_cast<long long>(num_n_blocks) * k_blocks;
+  if (S * P >= (1ll << 31)) return 0;
+  return P;
+}
+
 int ensure_sk_workspace(pf_ctx *c, int workers) {
-  const size_t ws = static_cast<size_t>(workers) * 2 * 128 * 256 * sizeof(float);
+  const size_t ws = static_cast<size_t>(workers) * 2 * 128 * c->var.partial_cols * sizeof(float);
   const size_t fl = static_cast<size_t>(workers) * 2 * sizeof(unsigned);
   if (c->sk_ws_cap < ws) {
     if (c->sk_ws) cudaFree(c->sk_ws);
@@ -570,7 +606,18 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     p.timeout_ns = c->timeout_ns;
     int workers = std::min(p.num_tiles, c->max_units);
     const int sk_tiles = sk_tail_tiles(c, p.num_tiles, p.k_blocks);
-    if (sk_tiles > 0) {
+    const int band_p = band_workers(c, p.num_m_blocks, p.num_n_blocks, p.k_blocks);
+    if (band_p > 0) {
+      // Row-band stream-K: P pairs per row block; one partial per pair (two CTAs x 128 x 512 fp32).
+      workers = p.num_m_blocks * band_p;
+      int rc;
+      if ((rc = ensure_sk_workspace(c, workers))) return rc;
+      if (++c->epoch == 0) c->epoch = 1;
+      p.sk_band_workers = band_p;
+      p.epoch = c->epoch;
+      p.sk_partials = c->sk_ws;
+      p.sk_flags = c->sk_flags;
+    } else if (sk_tiles > 0) {
       // Stream-K tail: whole waves stay data-parallel, the last sk_tiles tiles' k-iterations are
       // shared by every resident pair.  Workspace: one 256 KB partial per pair (two CTAs x 128 x 256 fp32).
       workers = c->max_units;
@@ -937,9 +984,12 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
   out->threads = c->var.threads;
   out->num_sms = c->num_sms;
   if (c->var.path == Path::kTensor) {
-    const int tiles = ((c->M + c->var.bm - 1) / c->var.bm) * ((c->N + c->var.bn - 1) / c->var.bn);
+    const int mblocks = (c->M + c->var.bm - 1) / c->var.bm, nblocks = (c->N + c->var.bn - 1) / c->var.bn;
+    const int tiles = mblocks * nblocks;
     const int kb = (c->K + c->var.bk_elems - 1) / c->var.bk_elems;
-    const int workers = sk_tail_tiles(c, tiles, kb) > 0 ? c->max_units : std::min(tiles, c->max_units);
+    const int band_p = band_workers(c, mblocks, nblocks, kb);
+    const int workers = band_p > 0 ? mblocks * band_p
+                                   : (sk_tail_tiles(c, tiles, kb) > 0 ? c->max_units : std::min(tiles, c->max_units));
     out->grid = workers * c->var.cta_per_tile;
   } else {
     out->grid = ((c->N + c->var.sbn - 1) / c->var.sbn) * ((c->M + c->var.sbm - 1) / c->var.sbm);

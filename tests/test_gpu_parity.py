@@ -457,7 +457,8 @@ def test_512_wide_tiles_at_full_size(ctx, oracle_mod, name, tile):
 
 @pytest.mark.parametrize("rows", [1024, 2048])
 def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
-    # the 8- and 4-GPU row shards of config 3, where default_tile picks 256 x 512 tiles
+    # the 8- and 4-GPU row shards of config 3, where default_tile picks 256 x 512 tiles (whole tiles: row-band
+    # stream-K is opt-in), and the same shards with row-band stream-K forced on (4 / 8 bands of 18 / 9 pairs)
     w = wl.CONFIGS["cfg3_bf16_8192"]
     ws = wl.scaled(w, rows, w.N, w.K)
     assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == pf.WIDE_TILE
@@ -465,9 +466,20 @@ def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
     A, B, bias, C = device_operands(ws, inp)
     run_pf(ctx, ws, inp, None, (A, B, bias, C))
     assert ctx.attrs()["threads"] == 320
+    assert ctx.attrs()["grid"] == 2 * min(74, (rows // 256) * 16)
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
     assert err <= TOL[ws.dtype]
-    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[ws.dtype]
+    ref = torch_fp32_reference(A, B, bias, 1.0)
+    assert max_rel_err_t(ref, C) <= TOL[ws.dtype]
+    ctx.set_stream_k(1)
+    try:
+        band = torch.full_like(C, float("nan"))
+        run_pf(ctx, ws, inp, None, (A, B, bias, band))
+        bands = rows // 256
+        assert ctx.attrs()["grid"] == 2 * bands * (74 // bands)
+    finally:
+        ctx.set_stream_k(-1)
+    assert max_rel_err_t(ref, band) <= TOL[ws.dtype]
 
 
 @pytest.mark.parametrize("tile", [WIDE, WIDE8])
@@ -510,3 +522,43 @@ def test_run_host_rows_equals_device_path(ctx, name, shape):
     want = C.reshape(-1).view(torch.uint8).cpu()
     assert torch.equal(hC, want)
     assert torch.equal(A2.reshape(-1).view(torch.uint8).cpu(), hA.reshape(-1).view(torch.uint8))
+
+
+# ---------------------------------------------------------------------------------------------
+# row-band stream-K of the 256 x 512 pair kernel: each row block of tiles shared by 74 // (row blocks) pairs
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name,shape,tile", [
+    ("cfg3_bf16_8192", (512, 2048, 1024), WIDE8),     # 2 bands of 37 pairs, ~1.7 k-blocks each: many contributors
+    ("cfg3_bf16_8192", (1024, 4608, 512), WIDE8),     # 4 bands of 18 pairs: 2-3 pairs per tile
+    ("cfg3_bf16_8192", (700, 1504, 600), WIDE8),      # ragged M, N and K
+    ("cfg3_bf16_8192", (1024, 4608, 512), WIDE),      # 4 epilogue warps (256 columns each per half)
+    ("cfg3_bf16_8192", (256, 8192, 2048), WIDE8),     # 1 band of 74 pairs
+    ("cfg5_e4m3_16384", (512, 2048, 2048), WIDE8),
+    ("cfg5_e4m3_16384", (1024, 4608, 1024), WIDE8)])
+def test_band_stream_k_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape, tile):
+    w = wl.scaled(wl.CONFIGS[name], *shape)
+    inp = wl.make_inputs(w, seed=59)
+    A, B, bias, C = device_operands(w, inp)
+    ctx.set_stream_k(1)
+    try:
+        run_pf(ctx, w, inp, tile, (A, B, bias, C))
+        bands = -(-w.M // 256)
+        assert ctx.attrs()["grid"] == 2 * bands * (74 // bands)
+        if w.M * w.N * w.K <= 2 ** 30:
+            check_full(oracle_mod, w, inp, C)
+        else:
+            assert int(torch.isnan(C.float()).sum()) == 0
+            err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), inp.scale_a * inp.scale_b,
+                                                samples=512, seed=99)
+            assert err <= TOL[w.dtype]
+            assert max_rel_err_t(torch_fp32_reference(A, B, bias, inp.scale_a * inp.scale_b), C) <= TOL[w.dtype]
+        again = torch.full_like(C, float("nan"))
+        run_pf(ctx, w, inp, tile, (A, B, bias, again))
+        assert torch.equal(C, again)  # deterministic for a given shape
+        ctx.set_stream_k(0)
+        whole = torch.full_like(C, float("nan"))
+        run_pf(ctx, w, inp, tile, (A, B, bias, whole))
+        assert ctx.attrs()["grid"] == 2 * min(74, bands * -(-w.N // 512))
+        assert max_rel_err_t(whole.float(), C.float()) <= TOL[w.dtype]
+    finally:
+        ctx.set_stream_k(-1)

@@ -55,5 +55,8 @@ def test_persistent_kernels_fit_one_cta_per_sm():
         if t is None:
             continue
         seen.add(t)
-        assert r["regs"] * t <= 65536, (name, r["regs"], t)
+        # the register file hands a warp its registers in blocks of 512 (16 per thread): 200 registers x 10 warps
+        # was refused at launch ("too many resources requested") though 200 x 320 < 65,536
+        per_warp = -(-r["regs"] * 32 // 512) * 512
+        assert per_warp * (t // 32) <= 65536, (name, r["regs"], t)
     assert {192, 320, 448} <= seen  # the 1-CTA / pair kernels, the 8-warp 256x512 kernel, 3xTF32

@@ -3,7 +3,8 @@ reference's search space that take its fallbacks (no GPU needed: nvcc cross-comp
 
 * BM + PAD not a multiple of 4: the transposed A tile's rows are not 16-byte multiples, so A is read with
   scalar loads (float4 reads there would be misaligned).
-* two stages above 48 KB of static shared memory: one stage, two barriers per K step.
+* the ring depth: up to 4 stages within the shared memory a CTA gets at its register-limited occupancy
+  (at most 48 KB of static shared memory); where two stages do not fit, one stage with two barriers per k step.
 The GPU side (bit-for-bit equality with a precompiled tile) is tests/test_gpu_image_runner.py.
 """
 import os
@@ -30,4 +31,8 @@ def test_fallback_tiles_compile_without_spills(tile, tmp_path):
     assert "0 bytes spill stores" in r.stderr
     smem = int(re.search(r"(\d+) bytes smem", r.stderr).group(1))
     stage = 4 * (BK * (BM + PAD) + BK * BN)
-    assert smem == (2 * stage if 2 * stage <= 48 * 1024 else stage)
+    threads = (BM // TM) * (BN // TN)
+    min_blocks = 512 // threads if TM * TN <= 64 and threads <= 512 else 1
+    budget = min(227 * 1024 // min_blocks - 1024, 48 * 1024)
+    fit = budget // stage
+    assert smem == stage * (4 if fit >= 4 else (fit if fit >= 2 else 1))

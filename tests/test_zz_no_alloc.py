@@ -97,12 +97,20 @@ def test_requests_it_cannot_serve_are_refused(pf):
     inp = wl.make_inputs(w)
     A, B, bias = _operands(w, inp)
     C = _nan_c(w)
+    # the C ABI's own refusals, reached with raw device pointers (a C caller's view: no shapes to check)
+    ptrs = [t.data_ptr() for t in (A, B, bias, C)]
     with pytest.raises(pf.PFError) as e:
-        pf.gemm_bias_gelu_noalloc(0, "f32", (128, 128, 8, 8, 8, 4), w.M, w.N, w.K, A, B, bias, C)
+        pf.gemm_bias_gelu_noalloc(0, "f32", (128, 128, 8, 8, 8, 4), w.M, w.N, w.K, *ptrs)
     assert e.value.code == pf.PF_EINVAL and "tensor-core" in str(e.value)
     with pytest.raises(pf.PFError) as e:
-        pf.gemm_bias_gelu_noalloc(0, "bf16", (64, 256, 32, 4, 16, 0), w.M, w.N, w.K, A, B, bias, C)
+        pf.gemm_bias_gelu_noalloc(0, "bf16", (64, 256, 32, 4, 16, 0), w.M, w.N, w.K, *ptrs)
     assert e.value.code == pf.PF_ETILE and "no tensor-core kernel" in str(e.value)
     with pytest.raises(pf.PFError) as e:
-        pf.gemm_bias_gelu_noalloc(0, "bf16", None, w.M, 100, w.K, A, B, bias, C)
+        pf.gemm_bias_gelu_noalloc(0, "bf16", None, w.M, 100, w.K, *ptrs)
     assert e.value.code == pf.PF_ESHAPE
+    other = torch.cuda.Stream()  # any stream of this device is accepted
+    other.wait_stream(torch.cuda.current_stream())
+    assert pf.gemm_bias_gelu_noalloc(0, "bf16", None, w.M, w.N, w.K, A, B, bias, C, stream=other) == 0
+    # torch operands whose shapes disagree with M, N, K never reach the C ABI
+    with pytest.raises(ValueError, match="but M, N, K"):
+        pf.gemm_bias_gelu_noalloc(0, "bf16", None, w.M, 128, w.K, A, B, bias, C)
