@@ -150,16 +150,17 @@ int pf_attrs(pf_ctx *ctx, pf_attr *out);
 int pf_device_status(pf_ctx *ctx, unsigned *err_word);
 
 /* Stream-K of the CTA-pair (BM=256) kernels: -1 auto (default), 0 off (every tile whole: results
- * independent of the launch shape, bit for bit), 1 on wherever the kernel can.
- *   - 256 x 256 pair tiles (and PF_F32_3XTF32): a stream-K tail -- the leftover tiles' k-iterations of a
- *     partial last wave are spread over all resident CTA pairs.  Auto: with at least 3 waves of tiles when the
- *     last partial wave would waste more than 3 % of the launch; PF_F32_3XTF32 also below that when whole tiles
- *     would leave a quarter of the CTA pairs idle, given 4 leftover k-blocks per pair.  1: whenever there is a
- *     partial wave.  Workspace: 256 KB per CTA pair.
- *   - 256 x 512 pair tiles: row-band stream-K -- each row block of tiles is shared by P = pairs / row blocks
- *     pairs, each taking an equal contiguous share of its k-iterations.  Auto: off (measured slower on the
- *     row shards it would serve: every extra unit boundary stalls the kernel's single accumulator); 1:
- *     wherever P >= 2.  Workspace: 512 KB per CTA pair.
+ * independent of the launch shape, bit for bit), 1 the stream-K tail wherever there is a partial wave,
+ * 2 row-band stream-K wherever a row block gets at least two pairs.
+ *   - Stream-K tail (256 x 256 pair tiles, PF_F32_3XTF32): the leftover tiles' k-iterations of a partial last
+ *     wave are spread over all resident CTA pairs.  Auto: with at least 3 waves of tiles when the last partial
+ *     wave would waste more than 3 % of the launch; PF_F32_3XTF32 also below that when whole tiles would
+ *     leave a quarter of the CTA pairs idle, given 4 leftover k-blocks per pair.  Workspace: 256 KB per pair.
+ *   - Row-band stream-K (256 x 256 and 256 x 512 pair tiles, mode 2 only): each row block of tiles is shared
+ *     by P = pairs / row blocks pairs, each taking an equal contiguous share of its k-iterations (pairs at the
+ *     same position of every band read the same B panel at the same time).  Measured no faster than whole
+ *     tiles on the row shards it was built for, so auto mode does not use it.  Workspace: 256 / 512 KB per
+ *     pair.
  * Split tiles' fp32 partial sums are added in a fixed order (deterministic for a given shape), but in a
  * different rounding from whole tiles. */
 int pf_set_stream_k(pf_ctx *ctx, int mode);

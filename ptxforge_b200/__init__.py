@@ -285,7 +285,8 @@ class Context:
         return w.value
 
     def set_stream_k(self, mode: int):
-        """Stream-K tail of the CTA-pair kernel: -1 auto (default), 0 off, 1 on (pf_set_stream_k)."""
+        """Stream-K of the CTA-pair kernels (pf_set_stream_k): -1 auto (default), 0 off (whole tiles), 1 the
+        stream-K tail, 2 row-band stream-K."""
         self._check(self._lib.pf_set_stream_k(self._h, mode), "pf_set_stream_k")
 
     def set_host_chunks(self, chunks: int):

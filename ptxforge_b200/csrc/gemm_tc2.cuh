@@ -16,7 +16,10 @@
 // Work units.  A pair ("worker") walks a list of units that all three roles enumerate identically
 // (sk_unit): first whole tiles, round-robin over the workers (data-parallel), then, when the launch
 // enables the stream-K tail (p.sk_iters > 0), a contiguous share of the k-iterations of the last
-// tiles, so a partial last wave does not leave SMs idle.  A tail tile is split between consecutive
+// tiles, so a partial last wave does not leave SMs idle.  Or, with p.sk_band_workers = P > 0 (row-band
+// stream-K), each row block of tiles is a band of P workers, each taking an equal contiguous share of the
+// band's k-iterations (band_unit); workers at the same position of different bands then read the same
+// B panel at the same k at the same time, so B comes from DRAM once for all bands.  A tail tile is split between consecutive
 // workers: the one holding the tile's first k-block ("head") finishes it; the others ("partials")
 // write their fp32 accumulators to a workspace and raise a flag tagged with the launch's epoch; the
 // head adds them in its epilogue.  A worker's partial is its first tail unit and its head its last,
@@ -67,17 +70,99 @@ struct Tc2Config {
 enum : int { kUnitWhole = 0, kUnitHead = 1, kUnitPartial = 2 };
 
 struct SkUnit {
-  int tile;      // global tile index (tile_coords order)
+  int tile;      // global tile index (tile_coords order); -1 in row-band mode
   int kb0, kb1;  // k-block range [kb0, kb1)
   int kind;      // kUnitWhole / kUnitHead / kUnitPartial
 };
 
-// Unit `u` of worker `w` of `W`; false past the worker's last unit.
-__device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, SkUnit &out) {
+// First k-iteration of band position j (of P) in a band of S k-iterations, floor(j * S / P), in 32-bit
+// arithmetic (S = q * P + r: j * q + j * r / P; the host keeps S * P below 2^31 in band mode).
+__device__ __forceinline__ int band_start(int j, int P, int S) { return j * (S / P) + (j * (S % P)) / P; }
+
+// Row-band stream-K (p.sk_band_workers = P > 0): worker w is position j = w % P of band (row block) g = w / P
+// and takes the band's k-iterations [band_start(j), band_start(j + 1)) -- its tiles left to right, k ascending.
+// Unit `u` of worker w, its tile (mb, nb); false past the worker's last unit.
+__device__ __forceinline__ bool band_unit(int w, int u, const TcParams &p, SkUnit &out, int &mb, int &nb) {
+  const int P = p.sk_band_workers;
+  const int g = w / P, j = w % P;
+  if (g >= p.num_m_blocks) return false;
+  const int KB = p.k_blocks;
+  const int S = p.num_n_blocks * KB;
+  const int e = band_start(j + 1, P, S);
+  int pos = band_start(j, P, S);
+  for (int i = 0; pos < e; ++i) {
+    const int t = pos / KB;
+    const int seg_end = min(e, (t + 1) * KB);
+    if (i == u) {
+      mb = g;
+      nb = t;
+      out.tile = -1;
+      out.kb0 = pos - t * KB;
+      out.kb1 = seg_end - t * KB;
+      out.kind = out.kb0 == 0 ? (out.kb1 == KB ? kUnitWhole : kUnitHead) : kUnitPartial;
+      return true;
+    }
+    pos = seg_end;
+  }
+  return false;
+}
+
+// The last worker whose partial a band-mode head at tile column nb adds: the band positions j' > j whose share
+// starts inside the tile, floor(j' S / P) < tile_end, i.e. j' < tile_end P / S.
+__device__ __forceinline__ int band_last_contributor(int w, int nb, const TcParams &p) {
+  const int P = p.sk_band_workers;
+  const int j = w % P;
+  const int S = p.num_n_blocks * p.k_blocks;
+  const int tile_end = (nb + 1) * p.k_blocks;
+  return w + min(P - 1, (tile_end * P + S - 1) / S - 1) - j;
+}
+
+// Folds the fp32 partials of `n_contrib` consecutive workers (slots `stride` float4 apart from `first`, this
+// lane's column-major layout: float4 index (col / 4) * 32 + lane) into this warp's 32 TMEM lanes: PIECES runs
+// of NCOLS columns, `piece_stride` apart from col_first, of the accumulator at t_row.  64 columns at a time:
+// both 32-column TMEM loads and all 16 partial loads of the first contributor in flight together, added in
+// worker order, stored back.
+template <int NCOLS, int PIECES = 1>
+__device__ __forceinline__ void fold_partials(uint32_t t_row, int col_first, int piece_stride, const float4 *first,
+                                              size_t stride, int n_contrib) {
+  static_assert(NCOLS % 64 == 0, "64-column steps");
+#pragma unroll 1
+  for (int c = 0; c < PIECES * (NCOLS / 64); ++c) {
+    const int col = col_first + (c / (NCOLS / 64)) * piece_stride + (c % (NCOLS / 64)) * 64;
+    uint32_t v[2][32];
+    tmem_ld_32x32b_x32(t_row + col, v[0]);
+    tmem_ld_32x32b_x32(t_row + col + 32, v[1]);
+    const float4 *src = first + (col / 4) * 32;
+#pragma unroll 1
+    for (int w = 0; w < n_contrib; ++w, src += stride) {
+      float4 s4[16];
+#pragma unroll
+      for (int j4 = 0; j4 < 16; ++j4) s4[j4] = __ldcg(src + j4 * 32);
+      if (w == 0) tmem_ld_wait();
+#pragma unroll
+      for (int j4 = 0; j4 < 16; ++j4) {
+        uint32_t *d = &v[j4 / 8][(j4 % 8) * 4];
+        d[0] = __float_as_uint(__uint_as_float(d[0]) + s4[j4].x);
+        d[1] = __float_as_uint(__uint_as_float(d[1]) + s4[j4].y);
+        d[2] = __float_as_uint(__uint_as_float(d[2]) + s4[j4].z);
+        d[3] = __float_as_uint(__uint_as_float(d[3]) + s4[j4].w);
+      }
+    }
+    if (n_contrib <= 0) tmem_ld_wait();
+    tmem_st_32x32b_x32(t_row + col, v[0]);
+    tmem_st_32x32b_x32(t_row + col + 32, v[1]);
+  }
+  tmem_st_wait();  // the folded sums are in TMEM before anything reads them back
+}
+
+// Unit `u` of worker `w` of `W` and its tile (mb, nb); false past the worker's last unit.
+__device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, SkUnit &out, int &mb, int &nb) {
+  if (p.sk_band_workers > 0) return band_unit(w, u, p, out, mb, nb);
   const int dp = p.sk_iters > 0 ? p.dp_tiles : p.num_tiles;
   const int n_dp = w < dp ? (dp - 1 - w) / W + 1 : 0;
   if (u < n_dp) {
     out = {w + u * W, 0, p.k_blocks, kUnitWhole};
+    tile_coords(out.tile, p, mb, nb);
     return true;
   }
   if (p.sk_iters <= 0) return false;
@@ -94,6 +179,7 @@ __device__ __forceinline__ bool sk_unit(int w, int W, int u, const TcParams &p, 
       out.kb0 = static_cast<int>(pos - local * KB);
       out.kb1 = static_cast<int>(seg_end - local * KB);
       out.kind = out.kb0 == 0 ? (out.kb1 == KB ? kUnitWhole : kUnitHead) : kUnitPartial;
+      tile_coords(out.tile, p, mb, nb);
       return true;
     }
     pos = seg_end;
@@ -181,6 +267,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
+  // writes global memory before that kernel is done.
+  grid_dependency_wait();
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -195,12 +284,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       bool ok = true;
       int issued = 0;
       SkUnit un;
-      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
-        int mb, nb;
-        tile_coords(un.tile, p, mb, nb);
+      int mb, nb;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, mb, nb); ++u) {
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::BN_CTA;
-        const bool reversed = tile_k_reversed(p, mb, nb, num_pairs);
+        const bool reversed = p.sk_band_workers == 0 && tile_k_reversed(p, mb, nb, num_pairs);
         for (int i = 0; i < un.kb1 - un.kb0; ++i) {
           const int kb = unit_kb(un, reversed, i);
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
@@ -234,6 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
       }
     }
+    grid_launch_dependents();  // this CTA's loads are all issued
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
@@ -243,7 +332,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       SkUnit un;
-      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
+      int mb, nb;
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, mb, nb); ++u) {
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
           ok = false;
@@ -289,8 +379,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       volatile int no_abort = 0;
       if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
     }
+    grid_launch_dependents();  // this CTA's MMAs are all issued (and, on the leader, complete)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
+    // A dependent launch may be scheduled once the producer and MMA warps are done (they signal last); its
+    // CTAs find SMs as this grid's CTAs exit, overlapping its launch and set-up with this tail.
+    grid_launch_dependents();
     const int q = warp & 3;
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;
@@ -304,9 +398,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       return reinterpret_cast<float4 *>(p.sk_partials + (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
                                         static_cast<size_t>(q) * 32 * Cfg::BN);
     };
-    for (int u = 0; sk_unit(pair, num_pairs, u, p, un); ++u) {
-      int mb, nb;
-      tile_coords(un.tile, p, mb, nb);
+    int mb, nb;
+    for (int u = 0; sk_unit(pair, num_pairs, u, p, un, mb, nb); ++u) {
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
@@ -349,10 +442,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         // Whole tile, or the head of a tail tile: add the later workers' partials (bounded waits).
         int first = 0, last = -1;
         if (un.kind == kUnitHead) {
-          const long long tile_end = static_cast<long long>(un.tile - p.dp_tiles + 1) * p.k_blocks;
           first = pair + 1;
-          last = pair;
-          while (last + 1 < num_pairs && sk_start(last + 1, num_pairs, p) < tile_end) ++last;
+          if (p.sk_band_workers > 0) {
+            last = band_last_contributor(pair, nb, p);
+          } else {
+            const long long tile_end = static_cast<long long>(un.tile - p.dp_tiles + 1) * p.k_blocks;
+            last = pair;
+            while (last + 1 < num_pairs && sk_start(last + 1, num_pairs, p) < tile_end) ++last;
+          }
           bool ok = true;
           if (lane == 0) {
             for (int w = first; w <= last && ok; ++w) {
@@ -371,6 +468,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             if (!ok) fail(kErrEpilogueWait);
           }
           if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+          for (int w = first; w <= last; ++w) (void)ld_acquire_gpu(p.sk_flags + w * 2 + rank);  // every lane
+          if constexpr (Cfg::BN % 64 == 0) {
+            if (p.sk_band_workers > 0) {
+              // Row-band mode: fold the partials into TMEM first (loads batched 64 columns at a time), then drain
+              // the tile as a whole one.
+              fold_partials<Cfg::BN>(t_row, 0, 0, slot(first) + lane, 2 * Cfg::PARTIAL_FLOATS / 4, last - pair);
+              first = last + 1;
+            }
+          }
         }
         auto addend = [&](uint32_t(&v)[32], int c0) {
           for (int w = first; w <= last; ++w) {

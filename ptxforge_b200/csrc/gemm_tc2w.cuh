@@ -79,9 +79,6 @@ struct WideUnit {
   bool reversed;  // whole tiles of odd waves walk k downwards (data-parallel schedule only)
 };
 
-// First k-iteration of band position j (of P) in a band of S k-iterations, floor(j * S / P), in 32-bit
-// arithmetic (S = q * P + r: j * q + j * r / P; the host keeps S below 2^31 in band mode).
-__device__ __forceinline__ int band_start(int j, int P, int S) { return j * (S / P) + (j * (S % P)) / P; }
 
 // Unit `u` of pair `w` of `W`; false past the pair's last unit.
 __device__ __forceinline__ bool wide_unit(int w, int W, int u, const TcParams &p, WideUnit &out) {
@@ -239,6 +236,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
+  // writes global memory before that kernel is done.
+  grid_dependency_wait();
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -289,6 +289,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
       }
     }
+    grid_launch_dependents();  // this CTA's loads are all issued
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
@@ -386,8 +387,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       volatile int no_abort = 0;
       if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
     }
+    grid_launch_dependents();  // this CTA's MMAs are all issued (and, on the leader, complete)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2.., both CTAs)
+    // A dependent launch may be scheduled once the producer and MMA warps are done (they signal last); its
+    // CTAs find SMs as this grid's CTAs exit, overlapping its launch and set-up with this tail.
+    grid_launch_dependents();
     const int q = warp & 3;                     // the TMEM lane quarter this warp may read
     const int ew = warp - 2;
     const int col0 = (ew / 4) * Cfg::EPI_COLS_WARP;  // its columns within each half
@@ -439,14 +444,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
       } else if (un.kind == kUnitHead) {
         // The first k-blocks of a tile whose later k-blocks the next pairs of this band summed: wait for their
-        // flags (bounded), then fold their partials into the accumulator.  They are the band positions j' > j
-        // whose share starts inside this tile: floor(j' S / P) < tile_end, i.e. j' < tile_end P / S (the host
-        // keeps S * P below 2^31).
-        const int P = p.sk_band_workers;
-        const int j = pair % P;
-        const int S = p.num_n_blocks * p.k_blocks;
-        const int tile_end = (un.nb + 1) * p.k_blocks;
-        const int last = pair + min(P - 1, (tile_end * P + S - 1) / S - 1) - j;
+        // flags (bounded), then fold their partials into the accumulator.
+        const int last = band_last_contributor(pair, un.nb, p);
         bool ok = true;
         if (lane == 0) {
           for (int w = pair + 1; w <= last && ok; ++w) {
@@ -466,38 +465,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
         for (int w = pair + 1; w <= last; ++w) (void)ld_acquire_gpu(p.sk_flags + w * 2 + rank);  // every lane
-        // Fold the partials of pairs [pair + 1, last] into this warp's accumulator rows in TMEM, 64 columns at a
-        // time: both 32-column TMEM loads and all 16 partial loads of the first contributor in flight together,
-        // add, store back; the tile then drains through the whole-tile epilogue below.
-        const float4 *first_slot = slot(pair + 1) + lane;
-        const int n_contrib = last - pair;
-#pragma unroll 1
-        for (int c = 0; c < 2 * Cfg::EPI_COLS_WARP / 64; ++c) {
-          const int col = (c / (Cfg::EPI_COLS_WARP / 64)) * Cfg::HALF_N + col0 + (c % (Cfg::EPI_COLS_WARP / 64)) * 64;
-          uint32_t v[2][32];
-          tmem_ld_32x32b_x32(t_row + col, v[0]);
-          tmem_ld_32x32b_x32(t_row + col + 32, v[1]);
-          const float4 *src = first_slot + (col / 4) * 32;
-#pragma unroll 1
-          for (int w = 0; w < n_contrib; ++w, src += 2 * Cfg::PARTIAL_FLOATS / 4) {
-            float4 s4[16];
-#pragma unroll
-            for (int j4 = 0; j4 < 16; ++j4) s4[j4] = __ldcg(src + j4 * 32);
-            if (w == 0) tmem_ld_wait();
-#pragma unroll
-            for (int j4 = 0; j4 < 16; ++j4) {
-              uint32_t *d = &v[j4 / 8][(j4 % 8) * 4];
-              d[0] = __float_as_uint(__uint_as_float(d[0]) + s4[j4].x);
-              d[1] = __float_as_uint(__uint_as_float(d[1]) + s4[j4].y);
-              d[2] = __float_as_uint(__uint_as_float(d[2]) + s4[j4].z);
-              d[3] = __float_as_uint(__uint_as_float(d[3]) + s4[j4].w);
-            }
-          }
-          if (n_contrib <= 0) tmem_ld_wait();
-          tmem_st_32x32b_x32(t_row + col, v[0]);
-          tmem_st_32x32b_x32(t_row + col + 32, v[1]);
-        }
-        tmem_st_wait();  // the folded sums are in TMEM before the epilogue below reads them back
+        // Fold the partials of pairs [pair + 1, last] into this warp's accumulator rows in TMEM (both of its
+        // 128-column pieces); the tile then drains through the whole-tile epilogue below.
+        fold_partials<Cfg::EPI_COLS_WARP, 2>(t_row, col0, Cfg::HALF_N, slot(pair + 1) + lane,
+                                             2 * Cfg::PARTIAL_FLOATS / 4, last - pair);
       }
       if (un.kind != kUnitPartial) {
         if constexpr (Cfg::EPI_COLS_WARP == 128) {

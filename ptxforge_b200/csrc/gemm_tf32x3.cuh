@@ -179,7 +179,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       bool ok = true;
       int issued = 0;
       SkUnit un;
-      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
+    int umb, unb;  // the unit's tile (this kernel reads it through tile_coords)
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
         int mb, nb;
         tile_coords(un.tile, p, mb, nb);
         const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
@@ -237,7 +238,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     uint32_t rphase = 0, sphase = 0;
     bool ok = true;
     SkUnit un;
-    for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
+    int umb, unb;  // the unit's tile (this kernel reads it through tile_coords)
+    for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
       for (int kb = un.kb0; kb < un.kb1; ++kb) {
         // 1. the raw slot's bytes, into registers
         bool waited = mbar_wait(&raw_full[rslot], rphase, p.timeout_ns, abort_flag);
@@ -308,7 +310,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       SkUnit un;
-      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un); ++u) {
+    int umb, unb;  // the unit's tile (this kernel reads it through tile_coords)
+      for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
           ok = false;
@@ -363,13 +366,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     uint32_t acc_phase = 0;
     int buf = 0;
     SkUnit un;
+    int umb, unb;  // the unit's tile (this kernel reads it through tile_coords)
     // This CTA's partial-sum slot (its 128 rows of a tile) in worker `w`'s workspace; a warp's 32 rows are
     // stored quad-of-columns-major so one warp-wide 16-byte access covers 512 contiguous bytes.
     auto slot = [&](int w) -> float4 * {
       return reinterpret_cast<float4 *>(p.sk_partials + (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
                                         static_cast<size_t>(q) * 32 * Cfg::BN);
     };
-    for (int u = 0; sk_unit(pair, num_pairs, u, p, un); ++u) {
+    for (int u = 0; sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
       int mb, nb;
       tile_coords(un.tile, p, mb, nb);
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);

@@ -13,9 +13,11 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "pf_b200.h"
@@ -74,6 +76,36 @@ struct Variant {
                       bool vec) = nullptr;
 };
 
+// Programmatic dependent launch for the CTA-pair kernels: each launch may be scheduled while the previous
+// kernel in the stream finishes; the kernel sets up its barriers and TMEM, then waits (griddepcontrol.wait)
+// for that kernel's completion before any global memory access, so the result is the same as a plain launch.
+// PF_PDL=0 in the environment turns it off (plain launches).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("PF_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <class... Params, class... Args>
+void launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, int smem, cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  cfg.numAttrs = 0;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  cfg.attrs = attr;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors surface through cudaGetLastError
+}
+
 template <int DT, int BN, int ST, int KA>
 void launch_tc_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                     const CUtensorMap &,
@@ -108,7 +140,7 @@ template <int DT, int ST, int KA, int BN>
 void launch_tc2_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                      const CUtensorMap &ct, const TcParams &p) {
   using Cfg = pf::Tc2Config<DT, ST, KA, BN>;
-  pf::gemm_bias_gelu_tc2<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, ct, p);
+  launch_pdl(&pf::gemm_bias_gelu_tc2<Cfg>, grid, Cfg::THREADS, Cfg::SMEM_BYTES, s, a, b, c, ct, p);
 }
 
 template <int DT, int ST, int KA = 1, int BN = 256>
@@ -130,6 +162,7 @@ Variant make_tc2_variant() {
   v.katoms = Cfg::KATOMS;
   v.cta_per_tile = 2;
   v.stream_k = true;
+  v.sk_band = BN % 64 == 0;  // row-band stream-K on 256-wide tiles (partials fold 64 columns at a time)
   v.launch_tc = &launch_tc2_impl<DT, ST, KA, BN>;
   return v;
 }
@@ -138,7 +171,7 @@ template <int DT, int ST, int EW>
 void launch_tc2w_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                       const CUtensorMap &, const TcParams &p) {
   using Cfg = pf::Tc2wConfig<DT, ST, EW>;
-  pf::gemm_bias_gelu_tc2w<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, c, p);
+  launch_pdl(&pf::gemm_bias_gelu_tc2w<Cfg>, grid, Cfg::THREADS, Cfg::SMEM_BYTES, s, a, b, c, p);
 }
 
 // CTA pairs with 256 x 512 tiles (gemm_tc2w.cuh): whole tiles, one k-atom per stage.
@@ -523,7 +556,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // us).  Below 2 waves the per-pair fixed costs (pipeline fill, the head's wait and partial reads, the
 // last epilogue) outweigh the rebalancing (1024-row shards: 105 -> 111 us), so auto stays data-parallel.
 int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
-  if (!c->var.stream_k || c->stream_k == 0) return 0;
+  if (!c->var.stream_k || c->stream_k == 0 || c->stream_k == 2) return 0;
   const int W = c->max_units;
   const int R = tiles % W;
   if (R == 0 || static_cast<long long>(R) * k_blocks < W) return 0;
@@ -537,22 +570,21 @@ int sk_tail_tiles(const pf_ctx *c, int tiles, int k_blocks) {
   return R;
 }
 
-// Pairs per band of a row-band stream-K launch of the 256 x 512 pair kernel (0 = whole tiles).  Each of the
-// launch's row blocks gets P = W / (row blocks) pairs, which share its k-iterations evenly, so the busiest pair
-// does ceil(S / P) k-blocks of the band's S instead of ceil(tiles / W) whole tiles' worth: on the 8- and 4-GPU
-// row shards of 8192^3 (4 and 8 bands of 18 and 9 pairs) 114 / 228 k-blocks per pair instead of 128 / 256.
-// Measured on B200 (CUDA events, bursts of 20 launches) it does not pay: 1,024 rows 99.7 -> 105.1 us, 2,048
-// rows 188.7 -> 190.9 us.  ncu of one launch each: the busy SMs' tensor pipes fall from 78.9 to 68.1 % of
-// cycles -- each pair runs two units instead of one, and with one 512-column accumulator per CTA every unit
-// boundary (and the partial's 256 KB drain per CTA, and the head's fold) stalls the MMAs for a few thousand
-// cycles, more than the 14 / 28 k-blocks saved.  So auto mode keeps whole tiles; 1 (pf_set_stream_k) runs it
-// wherever P >= 2 (tested against the oracle and against whole tiles).
+// Pairs per band of a row-band stream-K launch of a CTA-pair kernel (0 = whole tiles), used only when asked for
+// (pf_set_stream_k 2).  Each of the launch's row blocks gets P = W / (row blocks) pairs, which share its
+// k-iterations evenly, so the busiest pair does ceil(S / P) k-blocks of the band's S instead of ceil(tiles /
+// W) whole tiles' worth: on the 8- and 4-GPU row shards of 8192^3 (4 and 8 bands of 18 and 9 pairs) 114 / 228
+// 512-wide k-blocks per pair instead of 128 / 256.  Measured on B200 (CUDA events, bursts of 20 launches,
+// us, whole tiles -> bands): 256 x 512 tiles 1,024 rows 100.7 -> 106.6, 2,048 rows 192.0 -> 193.3; 256 x 256
+// tiles 105.2 -> 106.2 and 196.6 -> 192.2.  With more SMs busy each runs its MMAs less often (ncu, 256 x 512 at
+// 1,024 rows: the busy SMs' tensor pipes 78.9 -> 68.1 % of cycles) and the split tiles add partial writes and
+// reads, so the whole-tile schedule stays the default.
 int band_workers(const pf_ctx *c, int num_m_blocks, int num_n_blocks, int k_blocks) {
-  if (!c->var.sk_band || c->stream_k <= 0) return 0;
+  if (!c->var.sk_band || c->stream_k != 2) return 0;
   const int W = c->max_units;
   const int P = W / num_m_blocks;
   if (P < 2) return 0;
-  // the kernel's band arithmetic is 32-bit: S * P < 2^31
+  // the kernels' band arithmetic is 32-bit: S * P < 2^31
   const long long S = static_cast<long long>(num_n_blocks) * k_blocks;
   if (S * P >= (1ll << 31)) return 0;
   return P;
@@ -785,7 +817,7 @@ int pf_prepare_image(pf_ctx *c, const void *image, size_t image_bytes, const cha
 const char *pf_last_error(const pf_ctx *c) { return c ? c->err.c_str() : "null context"; }
 
 int pf_set_stream_k(pf_ctx *c, int mode) {
-  if (!c || mode < -1 || mode > 1) return set_err(c, PF_EINVAL, "stream-K mode must be -1, 0 or 1");
+  if (!c || mode < -1 || mode > 2) return set_err(c, PF_EINVAL, "stream-K mode must be -1, 0, 1 or 2");
   c->stream_k = mode;
   return PF_OK;
 }

@@ -189,6 +189,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Programmatic dependent launch.  grid_dependency_wait: every grid this launch depends on has completed and its
+// memory is visible (returns at once for a launch without the programmatic attribute).  grid_launch_dependents:
+// a dependent launched with that attribute may be scheduled once every CTA of this grid has signalled (or
+// exited); it still waits for this grid's completion before touching memory.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Warp-wide registers -> TMEM, the inverse of tmem_ld_32x32b_x32.
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(

@@ -471,7 +471,7 @@ def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
     assert err <= TOL[ws.dtype]
     ref = torch_fp32_reference(A, B, bias, 1.0)
     assert max_rel_err_t(ref, C) <= TOL[ws.dtype]
-    ctx.set_stream_k(1)
+    ctx.set_stream_k(2)
     try:
         band = torch.full_like(C, float("nan"))
         run_pf(ctx, ws, inp, None, (A, B, bias, band))
@@ -525,9 +525,16 @@ def test_run_host_rows_equals_device_path(ctx, name, shape):
 
 
 # ---------------------------------------------------------------------------------------------
-# row-band stream-K of the 256 x 512 pair kernel: each row block of tiles shared by 74 // (row blocks) pairs
+# row-band stream-K of the pair kernels: each row block of tiles shared by 74 // (row blocks) pairs
 # ---------------------------------------------------------------------------------------------
+PAIR256 = (256, 256, 32, 8, 16, 1)   # 256 x 256 pair tiles, two k-atoms per stage
+
+
 @pytest.mark.parametrize("name,shape,tile", [
+    ("cfg3_bf16_8192", (512, 2048, 1024), PAIR256),   # 256 x 256 tiles: 2 bands of 37 pairs
+    ("cfg3_bf16_8192", (1024, 4096, 1024), PAIR256),  # 4 bands of 18 pairs: 2-3 pairs per tile
+    ("cfg3_bf16_8192", (700, 1504, 600), PAIR256),    # ragged M, N and K
+    ("cfg5_e4m3_16384", (1024, 2048, 2048), PAIR256),
     ("cfg3_bf16_8192", (512, 2048, 1024), WIDE8),     # 2 bands of 37 pairs, ~1.7 k-blocks each: many contributors
     ("cfg3_bf16_8192", (1024, 4608, 512), WIDE8),     # 4 bands of 18 pairs: 2-3 pairs per tile
     ("cfg3_bf16_8192", (700, 1504, 600), WIDE8),      # ragged M, N and K
@@ -539,7 +546,7 @@ def test_band_stream_k_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape, t
     w = wl.scaled(wl.CONFIGS[name], *shape)
     inp = wl.make_inputs(w, seed=59)
     A, B, bias, C = device_operands(w, inp)
-    ctx.set_stream_k(1)
+    ctx.set_stream_k(2)
     try:
         run_pf(ctx, w, inp, tile, (A, B, bias, C))
         bands = -(-w.M // 256)
@@ -558,7 +565,26 @@ def test_band_stream_k_vs_oracle_and_whole_tiles(ctx, oracle_mod, name, shape, t
         ctx.set_stream_k(0)
         whole = torch.full_like(C, float("nan"))
         run_pf(ctx, w, inp, tile, (A, B, bias, whole))
-        assert ctx.attrs()["grid"] == 2 * min(74, bands * -(-w.N // 512))
+        assert ctx.attrs()["grid"] == 2 * min(74, bands * -(-w.N // tile[1]))
         assert max_rel_err_t(whole.float(), C.float()) <= TOL[w.dtype]
     finally:
         ctx.set_stream_k(-1)
+
+
+def test_band_stream_k_on_the_8_gpu_shard(ctx, oracle_mod, pf):
+    # 1,024 x 8192 x 8192 on 256 x 256 tiles: whole tiles need two waves (128 tiles, 74 pairs); row-band mode
+    # splits each of the 4 row blocks' k-iterations over 18 pairs instead
+    w = wl.scaled(wl.CONFIGS["cfg3_bf16_8192"], 1024, 8192, 8192)
+    inp = wl.make_inputs(w, seed=61)
+    A, B, bias, C = device_operands(w, inp)
+    run_pf(ctx, w, inp, PAIR256, (A, B, bias, C))
+    assert ctx.attrs()["grid"] == 148  # auto: whole tiles
+    ctx.set_stream_k(2)
+    try:
+        run_pf(ctx, w, inp, PAIR256, (A, B, bias, C))
+        assert ctx.attrs()["grid"] == 2 * 4 * 18
+    finally:
+        ctx.set_stream_k(-1)
+    err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, to_np(C), samples=512, seed=99)
+    assert err <= TOL[w.dtype]
+    assert max_rel_err_t(torch_fp32_reference(A, B, bias, 1.0), C) <= TOL[w.dtype]
