@@ -56,10 +56,10 @@ class Attr(ctypes.Structure):
 # Base tiles per dtype (default_tile() picks by shape from these and WIDE_TILE).  Tensor path: CTA pair (BM=256) x BN=256, two 128-byte k-atoms per
 # stage (PAD=1) and as many stages as fit (TM=8 -> 3), raster group 16 M-blocks (TN=16; with the pair kernel's
 # alternating k direction the least DRAM traffic: 0.95 GB per bf16 8192^3 launch vs 1.20 GB at TN=8) -- the lowest energy
-# per launch under the 1 kW cap; fp32: 128x128x8 block tile, 8x8 micro-tile, pad 4; 3xTF32: CTA pair,
+# per launch under the 1 kW cap; fp32: 128x64x16 block tile, 8x8 micro-tile, fed by TMA (large problems); 3xTF32: CTA pair,
 # 2 raw + 2 split slots (depth 4), raster group 8.
 DEFAULT_TILES = {
-    "f32": (128, 128, 8, 8, 8, 4),
+    "f32": (128, 64, 16, 8, 8, 0),
     "f32_3xtf32": (256, 256, 32, 4, 8, 0),
     "bf16": (256, 256, 32, 8, 16, 1),
     "e4m3": (256, 256, 32, 8, 16, 1),
@@ -82,18 +82,19 @@ def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int
     wave is nearly empty and 224-wide tiles add no wave: MLP shards of 2048 x 14336 (448 tiles, 4 in the last
     wave of 74 pairs) ran 6 % faster with 224; 8192-column shards of 1024 / 2048 rows and MLP shards of 4096
     rows ran 1.6-3.7 % slower.
-    f32: the SIMT kernel gives the same bits on every tile; small problems get small tiles.
+    f32: every SIMT tile gives the same bits (the reference kernel's fmaf chain); small problems get small tiles,
+    larger ones the TMA-fed kernel's 8-row micro-tiles.  Measured TFLOP/s at n^3 (CUDA events, B200): 512: 16.2 on
+    32 x 32 x 32 (TMA-fed 32 x 32: 14.4); 1024: 30.8 on 64 x 32 x 16 (t8x4, TMA) vs 29.1 on 64 x 64 x 16 (t4x4);
+    2048: 44.3 on 64 x 32 x 16 (TMA) vs 38.3 on 128 x 128 x 8 (t8x8); 4096: 47.9 on 128 x 64 x 16 (TMA) vs 45.4.
     """
     base = DEFAULT_TILES[dtype]
     if dtype == "f32":
-        # The 128 x 128 default only fills the GPU from about 128 of its tiles.  Measured (TFLOP/s, n^3):
-        # 512: 14.4 on 32 x 32 vs 4.0; 1024: 26.8 on 64 x 64 vs 16.8; 1536: 39.1 on 128 x 128 vs 34.3 on 64 x 64.
         t128 = -(-rows // 128) * -(-N // 128)
         if t128 < 48:
             return (32, 32, 32, 4, 2, 2)
-        if t128 < 128:
-            return (64, 64, 16, 4, 4, 4)
-        return base
+        if t128 < 512:
+            return (64, 32, 16, 8, 4, 0)
+        return (128, 64, 16, 8, 8, 0)
     if dtype not in ("bf16", "e4m3") or base[0] != 256:
         return base
     t256 = -(-rows // 256) * -(-N // 256)

@@ -22,6 +22,7 @@
 
 #include "pf_b200.h"
 #include "gemm_simt.cuh"
+#include "gemm_simt_tma.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "gemm_tc2w.cuh"
@@ -74,6 +75,12 @@ struct Variant {
   int sbm = 0, sbn = 0;
   void (*launch_simt)(dim3, cudaStream_t, const float *, const float *, const float *, float *, int, int, int,
                       bool vec) = nullptr;
+  // simt path fed by TMA (gemm_simt_tma.cuh), where the operands allow it: kernel, its dynamic shared memory,
+  // BK, and launcher (grid, stream, A map, B map, bias, C, M, N, K, status word, wait bound)
+  const void *tma_func = nullptr;
+  int tma_smem = 0, tma_bk = 0;
+  void (*launch_simt_tma)(dim3, cudaStream_t, const CUtensorMap &, const CUtensorMap &, const float *, float *, int,
+                          int, int, unsigned *, unsigned long long) = nullptr;
 };
 
 // Programmatic dependent launch for the CTA-pair kernels: each launch may be scheduled while the previous
@@ -260,6 +267,28 @@ Variant make_simt_variant() {
   return v;
 }
 
+template <int BM, int BN, int BK, int TM, int TN, int STAGES>
+void launch_simt_tma_impl(dim3 grid, cudaStream_t s, const CUtensorMap &a, const CUtensorMap &b, const float *bias,
+                          float *C, int M, int N, int K, unsigned *status, unsigned long long timeout_ns) {
+  using Cfg = pf::SimtTmaConfig<BM, BN, BK, TM, TN, STAGES>;
+  pf::gemm_bias_gelu_simt_tma<BM, BN, BK, TM, TN, STAGES>
+      <<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(a, b, bias, C, M, N, K, status, timeout_ns);
+}
+
+// The TMA-fed SIMT kernel for a tile, with the cp.async kernel of the same tile for operands TMA cannot
+// address (rows not 16-byte multiples, unaligned pointers) and for row-window launches; both give the same
+// bits.
+template <int BM, int BN, int BK, int TM, int TN, int PAD, int STAGES>
+Variant make_simt_tma_variant() {
+  using Cfg = pf::SimtTmaConfig<BM, BN, BK, TM, TN, STAGES>;
+  Variant v = make_simt_variant<BM, BN, BK, TM, TN, PAD>();
+  v.tma_func = reinterpret_cast<const void *>(&pf::gemm_bias_gelu_simt_tma<BM, BN, BK, TM, TN, STAGES>);
+  v.tma_smem = Cfg::SMEM_BYTES;
+  v.tma_bk = BK;
+  v.launch_simt_tma = &launch_simt_tma_impl<BM, BN, BK, TM, TN, STAGES>;
+  return v;
+}
+
 struct SimtEntry {
   pf_tile tile;
   Variant (*make)();
@@ -292,6 +321,16 @@ const SimtEntry kSimtTable[] = {
     {{32, 32, 8, 4, 4, 4}, &make_simt_variant<32, 32, 8, 4, 4, 4>},
     {{32, 32, 16, 4, 4, 4}, &make_simt_variant<32, 32, 16, 4, 4, 4>},
     {{32, 32, 32, 4, 4, 4}, &make_simt_variant<32, 32, 32, 4, 4, 4>},
+    // TMA-fed (gemm_simt_tma.cuh; PAD 0: A is not transposed, the TMA swizzle spreads its reads over the banks).
+    // The ring depth fits the shared memory a CTA gets at its register-limited occupancy.
+    {{64, 64, 16, 8, 8, 0}, &make_simt_tma_variant<64, 64, 16, 8, 8, 0, 3>},
+    {{64, 64, 32, 8, 8, 0}, &make_simt_tma_variant<64, 64, 32, 8, 8, 0, 2>},
+    {{128, 128, 16, 8, 8, 0}, &make_simt_tma_variant<128, 128, 16, 8, 8, 0, 4>},
+    {{128, 64, 16, 8, 8, 0}, &make_simt_tma_variant<128, 64, 16, 8, 8, 0, 4>},
+    {{64, 128, 16, 8, 8, 0}, &make_simt_tma_variant<64, 128, 16, 8, 8, 0, 4>},
+    {{64, 32, 16, 8, 4, 0}, &make_simt_tma_variant<64, 32, 16, 8, 4, 0, 3>},
+    {{32, 64, 16, 4, 8, 0}, &make_simt_tma_variant<32, 64, 16, 4, 8, 0, 3>},
+    {{32, 32, 16, 4, 4, 0}, &make_simt_tma_variant<32, 32, 16, 4, 4, 0, 6>},
 };
 
 bool same_tile(const pf_tile &a, const pf_tile &b) {
@@ -415,6 +454,7 @@ struct pf_ctx {
   float sa = 1.f, sb = 1.f;
   CUtensorMap tmA{}, tmB{}, tmC{}, tmCt{};  // tmCt: 32-column C boxes for the last columns of 224-wide tiles
   bool simt_vec = false;
+  bool simt_tma = false;  // the bound fp32 operands go through the TMA-fed kernel (maps in tmA / tmB)
   CUmodule module = nullptr;  // image loaded by pf_prepare_image
 
   // cuBLAS comparator state (pf_time_cublas): handle, workspace, GEMM output, transposed fp8 B, scales
@@ -676,8 +716,12 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     if (r != CUDA_SUCCESS) return set_err(c, PF_ECUDA, "cuLaunchKernel -> %s", cu_err(r));
   } else {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (c->M + v.sbm - 1) / v.sbm);
-    v.launch_simt(grid, s, static_cast<const float *>(c->A), static_cast<const float *>(c->B), c->bias,
-                  static_cast<float *>(c->C), c->M, c->N, c->K, c->simt_vec);
+    if (c->simt_tma)
+      v.launch_simt_tma(grid, s, c->tmA, c->tmB, c->bias, static_cast<float *>(c->C), c->M, c->N, c->K, c->d_status,
+                        c->timeout_ns);
+    else
+      v.launch_simt(grid, s, static_cast<const float *>(c->A), static_cast<const float *>(c->B), c->bias,
+                    static_cast<float *>(c->C), c->M, c->N, c->K, c->simt_vec);
   }
   PF_CUDA(c, cudaGetLastError());
   return PF_OK;
@@ -772,6 +816,7 @@ int pf_prepare_image(pf_ctx *c, const void *image, size_t image_bytes, const cha
   if (!c || !image || !image_bytes || !kernel) return set_err(c, PF_EINVAL, "null argument");
   c->prepared = false;
   c->bound = false;
+  c->simt_tma = false;
   if (M <= 0 || N <= 0 || K <= 0 || grid_x <= 0 || grid_y <= 0 || block <= 0)
     return set_err(c, PF_EINVAL, "sizes and launch shape must be positive");
   const DriverApi &api = driver_api();
@@ -838,6 +883,7 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
   if (!c || !t) return set_err(c, PF_EINVAL, "null argument");
   c->prepared = false;
   c->bound = false;
+  c->simt_tma = false;  // decided again when operands are bound
   if (M <= 0 || N <= 0 || K <= 0) return set_err(c, PF_EINVAL, "M, N, K must be positive (got %d, %d, %d)", M, N, K);
   DeviceGuard g(c->device);
   Variant v;
@@ -883,6 +929,10 @@ int pf_prepare(pf_ctx *c, pf_dtype dt, const pf_tile *t, int M, int N, int K) {
     c->group_m = t->TN;
   } else {
     return set_err(c, PF_ETILE, "dtype %d is not built in this library", (int)dt);
+  }
+  if (v.path == Path::kSimt && v.tma_func) {
+    cudaError_t e = cudaFuncSetAttribute(v.tma_func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.tma_smem);
+    if (e != cudaSuccess) return set_err(c, PF_ECUDA, "cudaFuncSetAttribute -> %s", cudaGetErrorString(e));
   }
   if (v.path == Path::kTensor) {
     cudaError_t e = cudaFuncSetAttribute(v.func, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
@@ -943,6 +993,18 @@ int pf_bind(pf_ctx *c, const void *A, const void *B, const float *bias, void *C,
   } else {
     c->simt_vec = aligned16(A) && aligned16(B) && aligned16(C) && aligned16(bias) && (c->K % 4 == 0) &&
                   (c->N % 4 == 0);
+    c->simt_tma = false;
+    if (c->simt_vec && c->var.tma_func) {
+      // A: [M x K] fp32, box BK x BM with the swizzle of one BK-float row; B: [K x N], box BN x BK, unswizzled.
+      const int bk = c->var.tma_bk;
+      int rc = encode_2d(c, &c->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, A, c->K, c->M, c->K * 4ull, bk, c->var.sbm,
+                         bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      rc = encode_2d(c, &c->tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, B, c->N, c->K, c->N * 4ull, c->var.sbn, bk,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      c->simt_tma = true;
+    }
   }
   c->bound = true;
   return PF_OK;
@@ -1003,15 +1065,19 @@ int pf_attrs(pf_ctx *c, pf_attr *out) {
     return PF_OK;
   }
   cudaFuncAttributes fa;
-  PF_CUDA(c, cudaFuncGetAttributes(&fa, c->var.func));
+  // the fp32 kernel that runs the bound operands (the TMA-fed one where they allow it)
+  const bool tma = c->simt_tma && c->var.tma_func && c->bound;
+  const void *fn = tma ? c->var.tma_func : c->var.func;
+  const int dyn_smem = tma ? c->var.tma_smem : c->var.smem;
+  PF_CUDA(c, cudaFuncGetAttributes(&fa, fn));
   int bps = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, c->var.func, c->var.threads, c->var.smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, fn, c->var.threads, dyn_smem) != cudaSuccess) {
     cudaGetLastError();  // cluster kernels: the per-SM query may be refused; one CTA per SM by construction
     bps = 1;
   }
   out->regs = fa.numRegs;
   out->local_bytes = static_cast<int>(fa.localSizeBytes);
-  out->smem_bytes = static_cast<int>(fa.sharedSizeBytes) + c->var.smem;
+  out->smem_bytes = static_cast<int>(fa.sharedSizeBytes) + dyn_smem;
   out->blocks_per_sm = bps;
   out->threads = c->var.threads;
   out->num_sms = c->num_sms;

@@ -79,7 +79,7 @@ def test_default_tile_choice_follows_the_measurements():
     assert pf.default_tile("bf16", 2048, 14336)[1] == 224      # MLP shard at 8 GPUs: 448 tiles, 4 in the last wave
     for rows, N in [(1024, 8192), (2048, 8192), (4096, 14336), (8192, 8192), (16384, 14336)]:
         assert pf.default_tile("bf16", rows, N) == pf.DEFAULT_TILES["bf16"], (rows, N)
-    assert pf.default_tile("f32", 2048, 2048) == pf.DEFAULT_TILES["f32"]
+    assert pf.default_tile("f32", 2048, 2048) == (64, 32, 16, 8, 4, 0)
     # 256 x 512 tiles for long tiles whose waves are full (1 GPU); the 256-wide kernel elsewhere
     assert pf.default_tile("bf16", 8192, 8192, 8192) == pf.WIDE_TILE          # 512 tiles, 128 k steps
     assert pf.default_tile("e4m3", 16384, 16384, 16384) == pf.WIDE_TILE       # 2048 tiles, 128 k steps
@@ -90,8 +90,10 @@ def test_default_tile_choice_follows_the_measurements():
     assert pf.default_tile("bf16", 2048, 8192, 8192) == pf.WIDE_TILE
     assert pf.default_tile("bf16", 4096, 8192, 8192) == pf.DEFAULT_TILES["bf16"]
     assert pf.default_tile("e4m3", 2048, 16384, 16384) == pf.DEFAULT_TILES["e4m3"]  # 3.5 vs 6.9 waves
-    # fp32 SIMT (same bits on every tile): small tiles while the 128 x 128 default would leave SMs idle
+    # fp32 SIMT (same bits on every tile): small tiles for small problems, the TMA-fed kernel's 64 x 32 tiles up to
+    # ~2900^2 outputs, 128 x 64 above
     assert pf.default_tile("f32", 512, 512) == (32, 32, 32, 4, 2, 2)
-    assert pf.default_tile("f32", 1024, 1024) == (64, 64, 16, 4, 4, 4)
-    assert pf.default_tile("f32", 1536, 1536) == pf.DEFAULT_TILES["f32"]
+    assert pf.default_tile("f32", 1024, 1024) == (64, 32, 16, 8, 4, 0)
+    assert pf.default_tile("f32", 1536, 1536) == (64, 32, 16, 8, 4, 0)
+    assert pf.default_tile("f32", 4096, 4096) == pf.DEFAULT_TILES["f32"]
     assert pf.default_tile("f32_3xtf32", 512, 512) == pf.DEFAULT_TILES["f32_3xtf32"]

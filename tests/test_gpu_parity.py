@@ -90,9 +90,12 @@ def max_rel_err_t(ref, C):
 FP32_TILES = [(128, 128, 8, 8, 8, 4), (128, 128, 8, 8, 8, 0), (128, 128, 16, 8, 8, 4), (128, 64, 8, 8, 4, 4),
               (64, 128, 8, 4, 8, 4), (64, 64, 8, 4, 4, 0), (64, 64, 8, 4, 4, 4), (64, 64, 16, 4, 4, 4),
               (32, 64, 8, 2, 4, 4), (32, 32, 8, 2, 2, 0)]
+# the TMA-fed kernel (gemm_simt_tma.cuh) on 16-byte-aligned operands, the cp.async kernel of the same tile elsewhere
+FP32_TMA_TILES = [(64, 64, 16, 8, 8, 0), (64, 64, 32, 8, 8, 0), (128, 128, 16, 8, 8, 0), (128, 64, 16, 8, 8, 0),
+                  (64, 128, 16, 8, 8, 0), (64, 32, 16, 8, 4, 0), (32, 64, 16, 4, 8, 0), (32, 32, 16, 4, 4, 0)]
 
 
-@pytest.mark.parametrize("tile", FP32_TILES)
+@pytest.mark.parametrize("tile", FP32_TILES + FP32_TMA_TILES)
 def test_fp32_cfg1_every_tile(ctx, oracle_mod, tile):
     w = wl.CONFIGS["cfg1_f32_512"]
     inp = wl.make_inputs(w)
@@ -103,7 +106,7 @@ def test_fp32_cfg1_every_tile(ctx, oracle_mod, tile):
 def test_fp32_ragged_shapes(ctx, oracle_mod, shape):
     w = wl.scaled(wl.CONFIGS["cfg1_f32_512"], *shape)
     inp = wl.make_inputs(w, seed=7)
-    for tile in [(128, 128, 8, 8, 8, 4), (64, 64, 8, 4, 4, 0)]:
+    for tile in [(128, 128, 8, 8, 8, 4), (64, 64, 8, 4, 4, 0), (64, 64, 16, 8, 8, 0), (32, 32, 16, 4, 4, 0)]:
         check_full(oracle_mod, w, inp, run_pf(ctx, w, inp, tile))
 
 
@@ -123,6 +126,10 @@ def test_fp32_bit_identical_to_reference_kernel(ctx, oracle_mod, ref_name):
         mine = run_pf(ctx, w, inp, None, (A, B, bias, C))
         torch.cuda.synchronize()
         assert torch.equal(mine, C_ref), f"{w.name}: differs from the reference kernel ({ref_name})"
+        for tile in FP32_TMA_TILES[:3] + FP32_TILES[:1]:  # TMA-fed and cp.async kernels, other tiles
+            again = torch.full_like(C, float("nan"))
+            run_pf(ctx, w, inp, tile, (A, B, bias, again))
+            assert torch.equal(again, C_ref), f"{w.name}, tile {tile}: differs from the reference kernel"
 
 
 def test_fp32_cfg2_gate_and_torch(ctx, oracle_mod):
