@@ -117,7 +117,7 @@ class B200Runner : public Runner {
   // atoms, so BK has no counterpart and is set to 32, and PAD (shared-memory padding in the SIMT kernel)
   // selects the stage layout: PAD=0 one k-atom per stage, PAD=1 or 8 two.  The search domain's columns
   // stop at 256 (space.hpp: BN in {32, 64, 128, 256}), so the 256 x 512 pair tiles are reached through
-  // BM=256, BN=256 with PAD=2 (8 epilogue warps, 3 stages) or PAD=4 (4 epilogue warps, 4 stages); every
+  // BM=256, BN=256 with PAD=2 (3 stages, two staging boxes per epilogue warp) or PAD=4 (4 stages, one); every
   // (BM, BN, TM, TN) the search proposes then reaches a kernel when one exists.  BM, BN, TM and TN keep the
   // meaning pf_b200.h gives them otherwise.  The fp32 path takes the Config as it is.
   pf_tile to_tile(const Config &c) const {

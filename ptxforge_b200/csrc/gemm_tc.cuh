@@ -289,6 +289,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
+  // writes global memory before that kernel is done.
+  grid_dependency_wait();
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -339,6 +342,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         }
       }
     }
+    grid_launch_dependents();  // this CTA's loads are all issued
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -395,8 +399,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       volatile int no_abort = 0;
       if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
     }
+    grid_launch_dependents();  // this CTA's MMAs are all issued and complete
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
+    grid_launch_dependents();  // a dependent launch waits for the producer and MMA warps, which signal last
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;

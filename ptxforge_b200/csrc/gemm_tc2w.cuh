@@ -36,7 +36,7 @@
 
 namespace pf {
 
-template <int kDtype, int kStages, int kEpiWarps = 4>
+template <int kDtype, int kStages, int kEpiWarps = 4, int kEpiBufs = 2>
 struct Tc2wConfig {
   static constexpr int BM = 256;                             // pair tile rows
   static constexpr int BM_CTA = 128;
@@ -59,7 +59,7 @@ struct Tc2wConfig {
   static constexpr int EPI_SPLIT = kEpiWarps / 4;            // warps sharing a quarter split its columns
   static constexpr int EPI_COLS_WARP = HALF_N / EPI_SPLIT;   // columns of a half each epilogue warp drains
   static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
-  static constexpr int EPI_BUFS = 2;
+  static constexpr int EPI_BUFS = kEpiBufs;                  // staging boxes per epilogue warp (1: 4 stages fit)
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1 + 1;
   static constexpr int TMEM_COLS = 512;                      // one accumulator: two halves of 256 columns
@@ -69,6 +69,7 @@ struct Tc2wConfig {
   static constexpr uint32_t IDESC =
       instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ HALF_N);
   static_assert(kEpiWarps == 4 || kEpiWarps == 8, "4 or 8 epilogue warps");
+  static_assert(kEpiBufs == 2 || (kEpiBufs == 1 && kEpiWarps == 8), "one staging box only with 8 epilogue warps");
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
   static_assert(B_CHUNKS_HALF >= 1, "each CTA supplies at least one 128-byte box of B per half");
 };
@@ -117,8 +118,8 @@ __device__ __forceinline__ bool wide_unit(int w, int W, int u, const TcParams &p
 // One epilogue warp's 32 rows x 128 columns of one accumulator half: the four 32-column TMEM loads first,
 // then the half is handed back (`release`) before any epilogue math, which runs from registers while the
 // next tile's MMAs already write that half; then x*scale + bias, GELU, bf16, two 32 x 64 boxes through the
-// double-buffered swizzled staging area and TMA stores, as epilogue_rows.
-template <class Release>
+// double-buffered (BUFS = 2) or single (1) swizzled staging area and TMA stores, as epilogue_rows.
+template <int BUFS = 2, class Release>
 __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, int n0, const TcParams &p,
                                                        const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
                                                        Release release) {
@@ -149,10 +150,10 @@ __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, i
     if (lane == 0) {
       if (n0 + b * 64 < p.N) tma_store_2d(tmC, ebuf + buf * BUF_BYTES, n0 + b * 64, m0);
       tma_store_commit();
-      tma_store_wait_read<1>();  // the other buffer is free again
+      tma_store_wait_read<BUFS - 1>();  // the buffer written next is free again
     }
     __syncwarp();
-    buf ^= 1;
+    if constexpr (BUFS == 2) buf ^= 1;
   }
 }
 
@@ -473,9 +474,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       if (un.kind != kUnitPartial) {
         if constexpr (Cfg::EPI_COLS_WARP == 128) {
           // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
-          epilogue_rows128_early(t_row + col0, m0, n_tile + col0, p, &tmC, ebuf, buf, lane, release0);
-          epilogue_rows128_early(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC, ebuf, buf,
-                                 lane, release1);
+          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, &tmC, ebuf, buf, lane, release0);
+          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
+                                                ebuf, buf, lane, release1);
         } else {
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, n_tile + col0, p, &tmC, nullptr, ebuf, buf, lane,
                                             release0);

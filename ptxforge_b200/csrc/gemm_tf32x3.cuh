@@ -165,6 +165,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
+  // writes global memory before that kernel is done.
+  grid_dependency_wait();
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -214,8 +217,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
       }
     }
+    grid_launch_dependents();  // this CTA's loads are all issued
   } else if (warp >= 2 + Cfg::EPI_WARPS) {
     // ---------------------------------------------------------------- split hi / lo (warps 6..13)
+    grid_launch_dependents();  // a dependent launch waits for the producer and MMA warps, which signal last
     constexpr int SPLIT_THREADS = 32 * Cfg::SPLIT_WARPS;
     constexpr int A_VEC = Cfg::A_BYTES / 16 / SPLIT_THREADS;   // 16-byte runs of A per thread
     constexpr int BLOCKS = 256 / SPLIT_THREADS;                // 4 x 4 blocks of B per thread
@@ -357,8 +362,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       volatile int no_abort = 0;
       if (!mbar_wait(drain, 0, p.timeout_ns, &no_abort)) atomicOr(p.status, kErrTeardownWait);
     }
+    grid_launch_dependents();  // this CTA's MMAs are all issued (and, on the leader, complete)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
+    grid_launch_dependents();
     const int q = warp & 3;
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;

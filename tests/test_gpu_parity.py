@@ -416,8 +416,8 @@ def test_224_wide_tiles_on_row_shards(ctx, oracle_mod, pf, name, rows):
 # ---------------------------------------------------------------------------------------------
 # 256 x 512 pair tiles (gemm_tc2w.cuh): one accumulator per CTA, handed back in two halves
 # ---------------------------------------------------------------------------------------------
-WIDE = (256, 512, 32, 4, 16, 0)      # 4 stages, 4 epilogue warps
-WIDE8 = (256, 512, 32, 3, 16, 0)     # 3 stages, 8 epilogue warps (two per TMEM lane quarter)
+WIDE = (256, 512, 32, 4, 16, 0)      # 4 stages, one staging box per epilogue warp
+WIDE8 = (256, 512, 32, 3, 16, 0)     # 3 stages, two staging boxes per epilogue warp (both: 8 epilogue warps)
 
 
 @pytest.mark.parametrize("name,shape", [("cfg3_bf16_8192", (512, 1024, 512)),
@@ -434,7 +434,7 @@ def test_512_wide_tiles_vs_oracle_and_256_wide(ctx, oracle_mod, name, shape, til
     inp = wl.make_inputs(w, seed=43)
     A, B, bias, C = device_operands(w, inp)
     run_pf(ctx, w, inp, tile, (A, B, bias, C))
-    assert ctx.attrs()["threads"] == (192 if tile == WIDE else 320)
+    assert ctx.attrs()["threads"] == 320
     assert ctx.attrs()["grid"] == 2 * min(74, -(-w.M // 256) * -(-w.N // 512))
     if w.M * w.N * w.K <= 2 ** 30:
         check_full(oracle_mod, w, inp, C)
@@ -468,7 +468,7 @@ def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
     # stream-K is opt-in), and the same shards with row-band stream-K forced on (4 / 8 bands of 18 / 9 pairs)
     w = wl.CONFIGS["cfg3_bf16_8192"]
     ws = wl.scaled(w, rows, w.N, w.K)
-    assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == pf.WIDE_TILE
+    assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == (pf.WIDE_TILE_DEEP if rows == 1024 else pf.WIDE_TILE)
     inp = wl.make_inputs(ws, seed=53)
     A, B, bias, C = device_operands(ws, inp)
     run_pf(ctx, ws, inp, None, (A, B, bias, C))
@@ -545,7 +545,7 @@ PAIR256 = (256, 256, 32, 8, 16, 1)   # 256 x 256 pair tiles, two k-atoms per sta
     ("cfg3_bf16_8192", (512, 2048, 1024), WIDE8),     # 2 bands of 37 pairs, ~1.7 k-blocks each: many contributors
     ("cfg3_bf16_8192", (1024, 4608, 512), WIDE8),     # 4 bands of 18 pairs: 2-3 pairs per tile
     ("cfg3_bf16_8192", (700, 1504, 600), WIDE8),      # ragged M, N and K
-    ("cfg3_bf16_8192", (1024, 4608, 512), WIDE),      # 4 epilogue warps (256 columns each per half)
+    ("cfg3_bf16_8192", (1024, 4608, 512), WIDE),      # 4 stages, one staging box per epilogue warp
     ("cfg3_bf16_8192", (256, 8192, 2048), WIDE8),     # 1 band of 74 pairs
     ("cfg5_e4m3_16384", (512, 2048, 2048), WIDE8),
     ("cfg5_e4m3_16384", (1024, 4608, 1024), WIDE8)])
