@@ -152,6 +152,7 @@ class ClockSampler:
 
     def __enter__(self):
         self.e0 = self.e1 = None
+        self.t0 = self.t1 = time.perf_counter()
         if self.ok:
             self.e0 = self._energy()
             self.t = threading.Thread(target=self._run, daemon=True)
@@ -159,6 +160,7 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        self.t1 = time.perf_counter()
         if self.ok:
             self._stop.set()
             self.t.join()
@@ -166,13 +168,17 @@ class ClockSampler:
 
     def energy(self, steps: int):
         """Energy of this GPU per step over the timed region (NVML's total-energy counter), or null with the
-        reason: the counter advances in coarse steps, so a region of a few milliseconds often reads zero."""
+        reason: the counter advances in coarse steps (tens of milliseconds), so over a region shorter than half
+        a second it reads zero or one step's worth -- neither is the region's energy."""
         src = "nvml total energy counter, this rank's GPU, over the timed region"
         if self.e0 is None or self.e1 is None or steps <= 0:
             return {"mj_per_step": None, "source": src, "reason": "counter unavailable"}
-        if self.e1 <= self.e0:
+        if self.t1 - self.t0 < 0.5:
             return {"mj_per_step": None, "source": src,
-                    "reason": "the counter did not advance during the timed region (too short for its update interval)"}
+                    "reason": f"timed region of {1e3 * (self.t1 - self.t0):.1f} ms is shorter than the counter's "
+                              "resolution allows (>= 500 ms)"}
+        if self.e1 <= self.e0:
+            return {"mj_per_step": None, "source": src, "reason": "the counter did not advance during the timed region"}
         return {"mj_per_step": round((self.e1 - self.e0) / steps, 1), "source": src}
 
     def summary(self):

@@ -61,9 +61,12 @@ def test_energy_and_clocks_print_null_with_a_reason():
     c = bench.ClockSampler.__new__(bench.ClockSampler)
     c.ok, c.samples, c.reasons, c.power, c.max_mhz = True, [], set(), [], 1965
     c.e0 = c.e1 = 1000
+    c.t0, c.t1 = 0.0, 2.0
     e = c.energy(20)
     assert e["mj_per_step"] is None and "did not advance" in e["reason"]
     s = c.summary()
     assert s["sm_mhz"] is None and s["samples"] == 0 and "no sample" in s["reason"]
     c.e1 = 3000
     assert c.energy(20)["mj_per_step"] == 100.0
+    c.t1 = 0.002  # a 20-step burst of 0.1 ms steps: one counter step would read as kilowatts
+    assert c.energy(20)["mj_per_step"] is None and "shorter" in c.energy(20)["reason"]
