@@ -59,6 +59,10 @@ struct TcParams {
   // ascending).  Pairs at the same position in different bands read the same B panel at the same time.
   // Partials go to sk_partials as [workers][2 CTAs][128 x 512] fp32; flags and epoch as above.
   int sk_band_workers = 0;
+  // Tail split (256 x 512 pair kernel only; 0 = off): in a pair's last whole tile, the second half's MMAs of the
+  // last min(tail_split, k_blocks / 2) k steps run after all of the first half's, so the epilogue drains the
+  // first half while the tensor pipe still works on the second.  Same k order per output: same bits.
+  int tail_split = 0;
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).
@@ -289,9 +293,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
-  // writes global memory before that kernel is done.
-  grid_dependency_wait();
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail.  The roles that touch
+  // global memory wait for that kernel to be done (griddepcontrol.wait) before their first access: the producer
+  // before its first load (its first unit's coordinates are worked out before), the epilogue on entry.  The MMA
+  // issuer touches only shared memory and TMEM.
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool dep_waited = false;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(t, p, mb, nb);
@@ -316,6 +322,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          if (!dep_waited) {
+            grid_dependency_wait();
+            dep_waited = true;
+          }
 #pragma unroll
           for (int a = 0; a < Cfg::KATOMS; ++a)
             tma_load_2d(sA + stage * Cfg::A_BYTES + a * Cfg::A_ATOM_BYTES, &tmA, &full[stage],
@@ -403,6 +413,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     grid_launch_dependents();  // a dependent launch waits for the producer and MMA warps, which signal last
+    grid_dependency_wait();
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;

@@ -267,9 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
-  // writes global memory before that kernel is done.
-  grid_dependency_wait();
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail.  The roles that touch
+  // global memory wait for that kernel to be done (griddepcontrol.wait) before their first access: the producer
+  // before its first load (its first unit's coordinates are worked out before), the epilogue on entry.  The MMA
+  // issuer touches only shared memory and TMEM.
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -297,6 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             break;
           }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          if (issued == 0) grid_dependency_wait();
           const uint32_t bar = pair_leader_addr(smem_u32(&full[stage]));
 #pragma unroll
           for (int a = 0; a < Cfg::KATOMS; ++a)
@@ -385,6 +387,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     // A dependent launch may be scheduled once the producer and MMA warps are done (they signal last); its
     // CTAs find SMs as this grid's CTAs exit, overlapping its launch and set-up with this tail.
     grid_launch_dependents();
+    grid_dependency_wait();
     const int q = warp & 3;
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;

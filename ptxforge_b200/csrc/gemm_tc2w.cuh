@@ -18,6 +18,10 @@
 //     each half released to the leader's `tempty[h]` right after its last TMEM load.  With 8 warps two
 //     share each 32-lane quarter of TMEM and split a half's 256 columns, so a half drains in about half the
 //     time: the tensor pipe waits on that drain at every tile boundary.
+//   * tail split: a pair's last tile has no next tile to hide its epilogue behind, and a 128 x 512 drain per
+//     CTA takes ~8 us.  So its last L k steps (p.tail_split) run half 0 first, then half 1 (A is loaded a
+//     second time for those steps); `tfull[0]` fires after half 0's last MMA and the epilogue drains half 0
+//     while the tensor pipe finishes half 1.  Every output still sums its k blocks in the same order.
 //
 // Work units.  Whole tiles round-robin over the pairs (k direction alternating by wave as in the other
 // kernels), or -- when p.sk_band_workers > 0 -- row-band stream-K: each row block of tiles is a band
@@ -61,7 +65,7 @@ struct Tc2wConfig {
   static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
   static constexpr int EPI_BUFS = kEpiBufs;                  // staging boxes per epilogue warp (1: 4 stages fit)
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BUF_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1 + 1;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1 + 1;
   static constexpr int TMEM_COLS = 512;                      // one accumulator: two halves of 256 columns
   static constexpr int PARTIAL_FLOATS = BM_CTA * BN;         // one CTA's share of a tile, fp32
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NUM_BARS * 8 + 16;
@@ -113,6 +117,27 @@ __device__ __forceinline__ bool wide_unit(int w, int W, int u, const TcParams &p
     pos = seg_end;
   }
   return false;
+}
+
+// k steps at the end of unit `u` (= un) of pair `w` whose half-1 MMAs follow all of half 0's (0: interleaved
+// throughout): only the pair's last whole tile, and at most half of its k steps.
+__device__ __forceinline__ int wide_tail_split(int w, int W, int u, const TcParams &p, const WideUnit &un) {
+  if (p.tail_split <= 0 || p.sk_band_workers > 0 || un.kind != kUnitWhole) return 0;
+  WideUnit next;
+  if (wide_unit(w, W, u + 1, p, next)) return 0;
+  return min(p.tail_split, (un.kb1 - un.kb0) / 2);
+}
+
+// The step order of a unit of S k steps with tail split L: steps j < S - L load and run both halves of k step
+// j; then S - L <= j < S half 0 only of k step j; then S <= j < S + L half 1 only of k step j - L.
+struct WideStep {
+  int i;       // the unit's k step (0 .. S-1, in the unit's k direction)
+  int halves;  // bit h: half h's B columns are loaded and its MMAs run
+};
+__device__ __forceinline__ WideStep wide_step(int j, int S, int L) {
+  if (j < S - L) return {j, 3};
+  if (j < S) return {j, 1};
+  return {j - L, 2};
 }
 
 // One epilogue warp's 32 rows x 128 columns of one accumulator half: the four 32-column TMEM loads first,
@@ -198,8 +223,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + Cfg::EPI_BYTES);
   uint64_t *full = bars;                        // [STAGES] leader: TMA bytes of both CTAs landed
   uint64_t *empty = bars + Cfg::STAGES;         // [STAGES] both: MMAs reading the stage finished
-  uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [1] both: accumulator ready
-  uint64_t *tempty = tfull + 1;                 // [2] leader: both CTAs drained half h
+  uint64_t *tfull = bars + 2 * Cfg::STAGES;     // [2] both: accumulator half h ready
+  uint64_t *tempty = tfull + 2;                 // [2] leader: both CTAs drained half h
   uint64_t *drain = tempty + 2;                 // [1] leader: all MMAs complete
   uint64_t *epi_sync = drain + 1;               // [1] the epilogue warps wrote this pair's partial
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_sync + 1);
@@ -219,7 +244,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       mbar_init(&full[s], 1);                   // the leader's producer arrives (with both CTAs' bytes)
       mbar_init(&empty[s], 1);                  // one multicast commit
     }
-    mbar_init(tfull, 1);
+    mbar_init(&tfull[0], 1);
+    mbar_init(&tfull[1], 1);
     mbar_init(&tempty[0], 2 * Cfg::EPI_WARPS);
     mbar_init(&tempty[1], 2 * Cfg::EPI_WARPS);
     mbar_init(drain, 1);
@@ -237,9 +263,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
-  // writes global memory before that kernel is done.
-  grid_dependency_wait();
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail.  The roles that touch
+  // global memory wait for that kernel to be done (griddepcontrol.wait) before their first access: the producer
+  // before its first load (its first unit's coordinates are worked out before), the epilogue on entry.  The MMA
+  // issuer touches only shared memory and TMEM.
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -257,23 +284,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       for (int u = 0; ok && wide_unit(pair, num_pairs, u, p, un); ++u) {
         const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA;
         const int n0 = un.nb * Cfg::BN + static_cast<int>(rank) * (Cfg::HALF_N / 2);
-        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
-          const int kb = un.reversed ? un.kb1 - 1 - i : un.kb0 + i;
+        const int S = un.kb1 - un.kb0;
+        const int L = wide_tail_split(pair, num_pairs, u, p, un);
+        for (int j = 0; j < S + L; ++j) {
+          const WideStep st = wide_step(j, S, L);
+          const int kb = un.reversed ? un.kb1 - 1 - st.i : un.kb0 + st.i;
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrProducerWait);
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full[stage],
+                                  2 * (Cfg::A_BYTES + (st.halves == 3 ? 2 : 1) * Cfg::B_HALF_BYTES));
+          if (issued == 0) grid_dependency_wait();
           const uint32_t bar = pair_leader_addr(smem_u32(&full[stage]));
           tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * Cfg::BK, m0);
           uint8_t *b_dst = sB + stage * Cfg::B_BYTES;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < 2; ++h) {
+            if (!((st.halves >> h) & 1)) continue;
 #pragma unroll
-            for (int j = 0; j < Cfg::B_CHUNKS_HALF; ++j)
-              tma_load_2d_pair(b_dst + h * Cfg::B_HALF_BYTES + j * Cfg::B_CHUNK_BYTES, &tmB, bar,
-                               n0 + h * Cfg::HALF_N + j * Cfg::B_CHUNK_N, kb * Cfg::BK);
+            for (int c = 0; c < Cfg::B_CHUNKS_HALF; ++c)
+              tma_load_2d_pair(b_dst + h * Cfg::B_HALF_BYTES + c * Cfg::B_CHUNK_BYTES, &tmB, bar,
+                               n0 + h * Cfg::HALF_N + c * Cfg::B_CHUNK_N, kb * Cfg::BK);
+          }
           ++issued;
           if (++stage == Cfg::STAGES) {
             stage = 0;
@@ -326,7 +361,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       };
       WideUnit un;
       for (int u = 0; ok && wide_unit(pair, num_pairs, u, p, un); ++u) {
-        const int steps = un.kb1 - un.kb0;
+        const int S = un.kb1 - un.kb0;
+        const int L = wide_tail_split(pair, num_pairs, u, p, un);
         // The first half of the accumulator must be drained of the previous unit.
         if (!mbar_wait_cluster(&tempty[0], tphase ^ 1u, p.timeout_ns, abort_flag)) {
           fail(kErrMmaWait);
@@ -337,34 +373,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         bool second_free = false;
         int pending = 0;  // stages whose second-half MMAs wait for the second half of TMEM
         int last = 0;
-        for (int i = 0; i < steps; ++i) {
+        for (int j = 0; j < S + L; ++j) {
+          const WideStep st = wide_step(j, S, L);
+          if (st.halves != 3 && (pending > 0 || !second_free)) {
+            // Entering the split tail: the second half is needed from here on, and stages held for it go first.
+            if (!second_free) {
+              if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
+                fail(kErrMmaWait);
+                ok = false;
+                break;
+              }
+              second_free = true;
+              tc_fence_after();
+            }
+            flush(pending, last, S - L - 1);
+            pending = 0;
+          }
           if (!mbar_wait(&full[stage], phase, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_half(stage, 0, i);
-          ++pending;
-          last = stage;
-          if (!second_free && mbar_test_wait_acq_cluster(tempty1_addr, tphase ^ 1u)) {
-            second_free = true;
-            tc_fence_after();
-          }
-          if (!second_free && pending == Cfg::STAGES) {
-            // Every stage is held: nothing more can load until the second half is free.
-            if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
-              fail(kErrMmaWait);
-              ok = false;
-              break;
+          if (st.halves == 3) {
+            issue_half(stage, 0, st.i);
+            ++pending;
+            last = stage;
+            if (!second_free && mbar_test_wait_acq_cluster(tempty1_addr, tphase ^ 1u)) {
+              second_free = true;
+              tc_fence_after();
             }
-            second_free = true;
-            tc_fence_after();
+            if (!second_free && pending == Cfg::STAGES) {
+              // Every stage is held: nothing more can load until the second half is free.
+              if (!mbar_wait_cluster(&tempty[1], tphase ^ 1u, p.timeout_ns, abort_flag)) {
+                fail(kErrMmaWait);
+                ok = false;
+                break;
+              }
+              second_free = true;
+              tc_fence_after();
+            }
+            if (second_free) {
+              flush(pending, last, st.i);
+              pending = 0;
+            }
+          } else {
+            // The split tail: one half per stage, the stage handed back right after it.
+            issue_half(stage, st.halves == 1 ? 0 : 1, st.i);
+            tc_commit_pair_mc(&empty[stage], 0x3);
           }
-          if (second_free) {
-            flush(pending, last, i);
-            pending = 0;
-          }
+          if (j == S - 1) tc_commit_pair_mc(&tfull[0], 0x3);  // every MMA of half 0 is issued
           if (++stage == Cfg::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -379,9 +437,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
             break;
           }
           tc_fence_after();
-          flush(pending, last, steps - 1);
+          flush(pending, last, S - 1);
         }
-        tc_commit_pair_mc(tfull, 0x3);
+        tc_commit_pair_mc(&tfull[1], 0x3);
         tphase ^= 1u;
       }
       tc_commit_pair(drain);
@@ -394,6 +452,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     // A dependent launch may be scheduled once the producer and MMA warps are done (they signal last); its
     // CTAs find SMs as this grid's CTAs exit, overlapping its launch and set-up with this tail.
     grid_launch_dependents();
+    grid_dependency_wait();
     const int q = warp & 3;                     // the TMEM lane quarter this warp may read
     const int ew = warp - 2;
     const int col0 = (ew / 4) * Cfg::EPI_COLS_WARP;  // its columns within each half
@@ -409,14 +468,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
                                         (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
                                         static_cast<size_t>(q) * 32 * Cfg::BN);
     };
-    WideUnit un;
-    for (int u = 0; wide_unit(pair, num_pairs, u, p, un); ++u) {
-      const bool waited = mbar_wait(tfull, tphase, p.timeout_ns, abort_flag);
+    // Whether accumulator half h of the current unit is complete (bounded wait, the whole warp agrees).
+    auto half_ready = [&](int h) -> bool {
+      const bool waited = mbar_wait(&tfull[h], tphase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
-        break;
+        return false;
       }
       tc_fence_after();
+      return true;
+    };
+    WideUnit un;
+    for (int u = 0; wide_unit(pair, num_pairs, u, p, un); ++u) {
+      if (!half_ready(0)) break;
+      bool second_ready = false;
       const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
       const int n_tile = un.nb * Cfg::BN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
@@ -430,6 +495,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         // This pair's first k-blocks of a tile another pair finishes: fp32 sums to the workspace, then the flag.
         float4 *dst = slot(pair);
         partial_rows<Cfg::EPI_COLS_WARP>(t_row + col0, dst + (col0 / 4) * 32, lane, release0);
+        if (!half_ready(1)) break;
         partial_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, dst + ((Cfg::HALF_N + col0) / 4) * 32, lane,
                                          release1);
         // Every warp's stores are visible device-wide before it arrives; one lane publishes the flag once
@@ -445,7 +511,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         }
       } else if (un.kind == kUnitHead) {
         // The first k-blocks of a tile whose later k-blocks the next pairs of this band summed: wait for their
-        // flags (bounded), then fold their partials into the accumulator.
+        // flags (bounded), then fold their partials into the accumulator (both halves).
+        if (!half_ready(1)) break;
+        second_ready = true;
         const int last = band_last_contributor(pair, un.nb, p);
         bool ok = true;
         if (lane == 0) {
@@ -475,11 +543,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
         if constexpr (Cfg::EPI_COLS_WARP == 128) {
           // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
           epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, &tmC, ebuf, buf, lane, release0);
+          if (!second_ready && !half_ready(1)) break;
           epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
                                                 ebuf, buf, lane, release1);
         } else {
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, n_tile + col0, p, &tmC, nullptr, ebuf, buf, lane,
                                             release0);
+          if (!second_ready && !half_ready(1)) break;
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
                                             nullptr, ebuf, buf, lane, release1);
         }

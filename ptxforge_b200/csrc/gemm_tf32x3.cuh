@@ -165,9 +165,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  // Under a programmatic launch the set-up above overlapped the previous kernel's tail; nothing below reads or
-  // writes global memory before that kernel is done.
-  grid_dependency_wait();
+  // Under a programmatic launch the set-up above overlapped the previous kernel's tail.  The roles that touch
+  // global memory wait for that kernel to be done (griddepcontrol.wait) before their first access: the producer
+  // before its first load (its first unit's coordinates are worked out before), the epilogue on entry.  The split
+  // warps and the MMA issuer touch only shared memory and TMEM.
 
   auto fail = [&](unsigned bit) {
     atomicOr(p.status, bit);
@@ -196,6 +197,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           }
           uint8_t *dst = sRaw + slot * Cfg::RAW_BYTES;
           mbar_arrive_expect_tx(&raw_full[slot], Cfg::RAW_BYTES);
+          if (issued == 0) grid_dependency_wait();
           tma_load_2d(dst, &tmA, &raw_full[slot], kb * Cfg::BK, m0);
 #pragma unroll
           for (int j = 0; j < Cfg::B_CHUNKS; ++j)
@@ -366,6 +368,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
     grid_launch_dependents();
+    grid_dependency_wait();
     const int q = warp & 3;
     const int ew = warp - 2;
     uint8_t *ebuf = sEpi + ew * Cfg::EPI_BUFS * Cfg::EPI_BUF_BYTES;

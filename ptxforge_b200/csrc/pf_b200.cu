@@ -95,6 +95,17 @@ bool pdl_enabled() {
   return on;
 }
 
+// Tail split of the 256 x 512 pair kernel (TcParams::tail_split): k steps at the end of each pair's last tile
+// whose second-half MMAs run after the first half's, so that the first half's epilogue overlaps them.
+// PF_TAIL_SPLIT=<steps> in the environment overrides the default (0 turns it off).
+int tail_split_steps() {
+  static const int steps = [] {
+    const char *e = std::getenv("PF_TAIL_SPLIT");
+    return e ? std::max(0, std::atoi(e)) : 8;
+  }();
+  return steps;
+}
+
 template <class... Params, class... Args>
 void launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, int smem, cudaStream_t s, Args &&...args) {
   cudaLaunchConfig_t cfg = {};
@@ -677,6 +688,7 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
+    p.tail_split = tail_split_steps();
     int workers = std::min(p.num_tiles, c->max_units);
     const int sk_tiles = sk_tail_tiles(c, p.num_tiles, p.k_blocks);
     const int band_p = band_workers(c, p.num_m_blocks, p.num_n_blocks, p.k_blocks);
@@ -1167,6 +1179,7 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
     p.group_m = std::max(1, std::min(c->group_m, p.num_m_blocks));
     p.status = c->d_status;
     p.timeout_ns = c->timeout_ns;
+    p.tail_split = tail_split_steps();
     // k directions as in one launch over the whole bound problem (the same bits as do_launch)
     const int full_m_blocks = (c->M + v.bm - 1) / v.bm;
     const int full_tiles = full_m_blocks * p.num_n_blocks;
@@ -1568,6 +1581,7 @@ extern "C" int pf_gemm_bias_gelu_noalloc(int device, pf_dtype dtype, const pf_ti
   p.group_m = std::max(1, std::min(t->TN, p.num_m_blocks));
   p.status = d.scratch;  // word 0 of the fixed scratch area
   p.timeout_ns = kNoallocWaitNs;
+  p.tail_split = tail_split_steps();
 
   ce = cudaMemsetAsync(d.scratch, 0, sizeof(unsigned), s);  // the last call's status must not leak in
   if (ce != cudaSuccess) return noalloc_fail(err, err_len, PF_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
