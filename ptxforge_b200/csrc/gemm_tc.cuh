@@ -147,20 +147,23 @@ struct NoAddend {
   __device__ __forceinline__ void operator()(uint32_t (&)[32], int) const {}
 };
 
-// 32 accumulator columns of one row (this lane's) -> x*scale + bias[c], GELU -> 16 packed bf16 pairs.
-__device__ __forceinline__ void epilogue_math32(const uint32_t (&v)[32], int n0, const TcParams &p,
-                                                uint32_t (&packed)[16]) {
+// 32 accumulator columns of one row (this lane's) -> x*scale + bias[c], GELU -> 16 packed bf16 pairs.  The
+// 32 columns' bias is held one per lane (lane j: column j) and broadcast by shuffles, so it is loaded ahead
+// (while the warp waits for the accumulator, or during the previous box), not between TMEM loads and stores.
+__device__ __forceinline__ void epilogue_math32_lane_bias(const uint32_t (&v)[32], float bias_lane, float scale,
+                                                          uint32_t (&packed)[16]) {
 #pragma unroll
-  for (int j4 = 0; j4 < 8; ++j4) {
-    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (n0 + j4 * 4 < p.N) b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + j4 * 4));
-    const float x0 = fmaf(__uint_as_float(v[j4 * 4 + 0]), p.scale, b4.x);
-    const float x1 = fmaf(__uint_as_float(v[j4 * 4 + 1]), p.scale, b4.y);
-    const float x2 = fmaf(__uint_as_float(v[j4 * 4 + 2]), p.scale, b4.z);
-    const float x3 = fmaf(__uint_as_float(v[j4 * 4 + 3]), p.scale, b4.w);
-    packed[j4 * 2 + 0] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
-    packed[j4 * 2 + 1] = pack_bf16x2(gelu_tanh_fast(x2), gelu_tanh_fast(x3));
+  for (int j = 0; j < 32; j += 2) {
+    const float x0 = fmaf(__uint_as_float(v[j]), scale, __shfl_sync(0xffffffffu, bias_lane, j));
+    const float x1 = fmaf(__uint_as_float(v[j + 1]), scale, __shfl_sync(0xffffffffu, bias_lane, j + 1));
+    packed[j / 2] = pack_bf16x2(gelu_tanh_fast(x0), gelu_tanh_fast(x1));
   }
+}
+
+// This lane's bias of columns col + lane and col + 32 + lane (0 past N): one 64-column box of a tile.
+__device__ __forceinline__ float2 lane_bias64(const TcParams &p, int col, int lane) {
+  const int c0 = col + lane, c1 = col + 32 + lane;
+  return make_float2(c0 < p.N ? __ldg(p.bias + c0) : 0.f, c1 < p.N ? __ldg(p.bias + c1) : 0.f);
 }
 
 // One epilogue warp turns its 32 accumulator rows x BN columns (TMEM lanes q*32.., columns from
@@ -170,18 +173,24 @@ __device__ __forceinline__ void epilogue_math32(const uint32_t (&v)[32], int n0,
 // `tmC_tail` (32 x 32 boxes, 64-byte swizzle), so a tile never writes into its neighbour's columns.
 // `release()` is called by the whole warp right after the last TMEM load of the tile; `addend(v, c0)`
 // may add other fp32 contributions to accumulator columns [c0, c0+32) before the epilogue math.
+// The bias travels one per lane (lane_bias64): the caller loads the first box's before the accumulator is
+// ready, and each box loads the next one's before its own TMEM loads.
 template <int BN, class Release, class Addend = NoAddend>
 __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile, const TcParams &p,
                                               const CUtensorMap *tmC, const CUtensorMap *tmC_tail, uint8_t *ebuf,
-                                              int &buf, int lane, Release release, Addend addend = Addend()) {
+                                              int &buf, int lane, float2 bias_first, Release release,
+                                              Addend addend = Addend()) {
   constexpr int EPI_COLS = 64;
   constexpr int BUF_BYTES = 32 * EPI_COLS * 2;
   constexpr int FULL = BN / EPI_COLS;
   constexpr bool TAIL = (BN % EPI_COLS) != 0;
   static_assert(BN % 32 == 0, "the epilogue works in 32-column steps");
+  float2 bias_next = bias_first;
 #pragma unroll 1
   for (int c = 0; c < FULL; ++c) {
     const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 128;
+    const float2 bias_box = bias_next;
+    if (c + 1 < FULL || TAIL) bias_next = lane_bias64(p, n_tile + (c + 1) * EPI_COLS, lane);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t v[32];
@@ -189,7 +198,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
       tmem_ld_wait();
       addend(v, c * EPI_COLS + h * 32);
       uint32_t packed[16];
-      epilogue_math32(v, n_tile + c * EPI_COLS + h * 32, p, packed);
+      epilogue_math32_lane_bias(v, h == 0 ? bias_box.x : bias_box.y, p.scale, packed);
       // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -223,7 +232,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, int m0, int n_tile
     release();
     addend(v, FULL * EPI_COLS);
     uint32_t packed[16];
-    epilogue_math32(v, n_tile + FULL * EPI_COLS, p, packed);
+    epilogue_math32_lane_bias(v, bias_next.x, p.scale, packed);
     // Row `lane` of the 32 x 32 box is 64 bytes; under the 64-byte swizzle its 16-byte chunk i lands at
     // chunk i ^ ((row / 2) % 4), which also spreads a quarter-warp's stores over all eight bank groups.
     const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 64;
@@ -423,6 +432,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
+      const float2 bias_first = lane_bias64(p, nb * Cfg::BN, lane);  // loaded while the accumulator fills
       // The TMEM loads below are warp-collective (.sync.aligned): the whole warp proceeds or leaves.
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
@@ -433,7 +443,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int m0 = mb * Cfg::BM + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
       uint64_t *tempty_acc = &tempty[acc];
-      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, nullptr, ebuf, buf, lane, [&] {
+      epilogue_rows<Cfg::BN>(t_row, m0, nb * Cfg::BN, p, &tmC, nullptr, ebuf, buf, lane, bias_first, [&] {
         if (lane == 0) mbar_arrive(tempty_acc);
       });
       if (++acc == 2) {

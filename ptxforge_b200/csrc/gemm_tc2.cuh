@@ -403,6 +403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     };
     int mb, nb;
     for (int u = 0; sk_unit(pair, num_pairs, u, p, un, mb, nb); ++u) {
+      const float2 bias_first = lane_bias64(p, nb * Cfg::BN, lane);  // loaded while the accumulator fills
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
@@ -495,7 +496,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           }
         };
         epilogue_rows<Cfg::BN>(
-            t_row, m0, nb * Cfg::BN, p, &tmC, &tmC_tail, ebuf, buf, lane,
+            t_row, m0, nb * Cfg::BN, p, &tmC, &tmC_tail, ebuf, buf, lane, bias_first,
             [&] {
               if (lane == 0) mbar_arrive_cluster(tempty_leader);
             },

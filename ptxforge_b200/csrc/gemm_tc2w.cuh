@@ -144,10 +144,11 @@ __device__ __forceinline__ WideStep wide_step(int j, int S, int L) {
 // then the half is handed back (`release`) before any epilogue math, which runs from registers while the
 // next tile's MMAs already write that half; then x*scale + bias, GELU, bf16, two 32 x 64 boxes through the
 // double-buffered (BUFS = 2) or single (1) swizzled staging area and TMA stores, as epilogue_rows.
+// bias_lane[c] is this lane's bias of column n0 + 32 c + lane (0 past N), loaded before the accumulator was ready.
 template <int BUFS = 2, class Release>
 __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, int n0, const TcParams &p,
-                                                       const CUtensorMap *tmC, uint8_t *ebuf, int &buf, int lane,
-                                                       Release release) {
+                                                       const float (&bias_lane)[4], const CUtensorMap *tmC,
+                                                       uint8_t *ebuf, int &buf, int lane, Release release) {
   constexpr int BUF_BYTES = 32 * 64 * 2;
   uint32_t v[4][32];
 #pragma unroll
@@ -162,7 +163,7 @@ __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, i
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t packed[16];
-      epilogue_math32(v[b * 2 + h], n0 + b * 64 + h * 32, p, packed);
+      epilogue_math32_lane_bias(v[b * 2 + h], bias_lane[b * 2 + h], p.scale, packed);
       // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -480,6 +481,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     };
     WideUnit un;
     for (int u = 0; wide_unit(pair, num_pairs, u, p, un); ++u) {
+      // This warp's bias columns of the unit's tile, one per lane, loaded while the accumulator fills.
+      float bias_lane[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int col = un.nb * Cfg::BN + h * Cfg::HALF_N + col0 + c * 32 + lane;
+          bias_lane[h][c] = (Cfg::EPI_COLS_WARP == 128 && col < p.N) ? __ldg(p.bias + col) : 0.f;
+        }
       if (!half_ready(0)) break;
       bool second_ready = false;
       const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
@@ -542,16 +552,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       if (un.kind != kUnitPartial) {
         if constexpr (Cfg::EPI_COLS_WARP == 128) {
           // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
-          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, &tmC, ebuf, buf, lane, release0);
+          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, bias_lane[0], &tmC, ebuf, buf, lane,
+                                                release0);
           if (!second_ready && !half_ready(1)) break;
-          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
-                                                ebuf, buf, lane, release1);
+          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p,
+                                                bias_lane[1], &tmC, ebuf, buf, lane, release1);
         } else {
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, n_tile + col0, p, &tmC, nullptr, ebuf, buf, lane,
-                                            release0);
+                                            lane_bias64(p, n_tile + col0, lane), release0);
           if (!second_ready && !half_ready(1)) break;
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p, &tmC,
-                                            nullptr, ebuf, buf, lane, release1);
+                                            nullptr, ebuf, buf, lane, lane_bias64(p, n_tile + Cfg::HALF_N + col0, lane),
+                                            release1);
         }
       }
       tphase ^= 1u;
