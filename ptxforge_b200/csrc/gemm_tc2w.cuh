@@ -144,10 +144,12 @@ __device__ __forceinline__ WideStep wide_step(int j, int S, int L) {
 // then the half is handed back (`release`) before any epilogue math, which runs from registers while the
 // next tile's MMAs already write that half; then x*scale + bias, GELU, bf16, two 32 x 64 boxes through the
 // double-buffered (BUFS = 2) or single (1) swizzled staging area and TMA stores, as epilogue_rows.
-// bias_lane[c] is this lane's bias of column n0 + 32 c + lane (0 past N), loaded before the accumulator was ready.
+// The bias travels one value per lane: `bias_lane` holds this lane's of column n0 + lane (loaded before the
+// accumulator was ready); each 32-column step loads the next step's, the last one that of column
+// next_col + lane (the next half's first step; none if next_col < 0), which is what `bias_lane` holds on return.
 template <int BUFS = 2, class Release>
 __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, int n0, const TcParams &p,
-                                                       const float (&bias_lane)[4], const CUtensorMap *tmC,
+                                                       float &bias_lane, int next_col, const CUtensorMap *tmC,
                                                        uint8_t *ebuf, int &buf, int lane, Release release) {
   constexpr int BUF_BYTES = 32 * 64 * 2;
   uint32_t v[4][32];
@@ -162,8 +164,11 @@ __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, i
     const uint32_t sbuf = smem_u32(ebuf + buf * BUF_BYTES) + lane * 128;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      const int col = (b * 2 + h < 3) ? n0 + (b * 2 + h + 1) * 32 + lane : (next_col < 0 ? p.N : next_col + lane);
+      const float bias_next = col < p.N ? __ldg(p.bias + col) : 0.f;
       uint32_t packed[16];
-      epilogue_math32_lane_bias(v[b * 2 + h], bias_lane[b * 2 + h], p.scale, packed);
+      epilogue_math32_lane_bias(v[b * 2 + h], bias_lane, p.scale, packed);
+      bias_lane = bias_next;
       // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -481,15 +486,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
     };
     WideUnit un;
     for (int u = 0; wide_unit(pair, num_pairs, u, p, un); ++u) {
-      // This warp's bias columns of the unit's tile, one per lane, loaded while the accumulator fills.
-      float bias_lane[2][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int col = un.nb * Cfg::BN + h * Cfg::HALF_N + col0 + c * 32 + lane;
-          bias_lane[h][c] = (Cfg::EPI_COLS_WARP == 128 && col < p.N) ? __ldg(p.bias + col) : 0.f;
-        }
+      // This lane's bias of the warp's first column of the unit's tile, loaded while the accumulator fills.
+      const int first_col = un.nb * Cfg::BN + col0 + lane;
+      float bias_lane = (Cfg::EPI_COLS_WARP == 128 && first_col < p.N) ? __ldg(p.bias + first_col) : 0.f;
       if (!half_ready(0)) break;
       bool second_ready = false;
       const int m0 = un.mb * Cfg::BM + static_cast<int>(rank) * Cfg::BM_CTA + q * 32;
@@ -552,11 +551,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       if (un.kind != kUnitPartial) {
         if constexpr (Cfg::EPI_COLS_WARP == 128) {
           // 128 columns fit in registers: each half goes back to the MMA issuer as soon as it is loaded.
-          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, bias_lane[0], &tmC, ebuf, buf, lane,
-                                                release0);
+          epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + col0, m0, n_tile + col0, p, bias_lane,
+                                                n_tile + Cfg::HALF_N + col0, &tmC, ebuf, buf, lane, release0);
           if (!second_ready && !half_ready(1)) break;
           epilogue_rows128_early<Cfg::EPI_BUFS>(t_row + Cfg::HALF_N + col0, m0, n_tile + Cfg::HALF_N + col0, p,
-                                                bias_lane[1], &tmC, ebuf, buf, lane, release1);
+                                                bias_lane, -1, &tmC, ebuf, buf, lane, release1);
         } else {
           epilogue_rows<Cfg::EPI_COLS_WARP>(t_row + col0, m0, n_tile + col0, p, &tmC, nullptr, ebuf, buf, lane,
                                             lane_bias64(p, n_tile + col0, lane), release0);
