@@ -63,6 +63,12 @@ struct TcParams {
   // last min(tail_split, k_blocks / 2) k steps run after all of the first half's, so the epilogue drains the
   // first half while the tensor pipe still works on the second.  Same k order per output: same bits.
   int tail_split = 0;
+  // Periodic promotion (3xTF32 kernel only; 0 = off): a unit's k range is summed in chunks of promote_kb k-blocks
+  // that alternate between the two TMEM accumulators, and the epilogue adds each finished chunk into an fp32
+  // running sum (round to nearest) in promote_ws ([workers][2 CTAs][128 x 256] fp32), so the tensor cores'
+  // round-toward-zero accumulation spans promote_kb k-blocks, not the whole k range.
+  int promote_kb = 0;
+  float *promote_ws = nullptr;
 };
 
 // kDtype: 0 = bf16 (kind::f16), 1 = e4m3 (kind::f8f6f4).

@@ -35,6 +35,13 @@
 // Work units are those of the CTA-pair kernel (sk_unit, gemm_tc2.cuh): whole tiles, then, with a stream-K
 // tail, contiguous k ranges of the last tiles spread over every pair; a tail tile's head pair adds the other
 // pairs' fp32 partial sums in its epilogue.  k always ascends inside a unit.
+// Periodic promotion (p.promote_kb > 0): the tensor cores accumulate fp32 with truncation (round toward zero),
+// so a long k range drifts toward zero -- by about 6.4e-9 x K relative on U(-0.5, 0.5) inputs, past 1e-5 from
+// K ~ 2048.  A unit's k range is therefore cut into chunks of promote_kb k-blocks that alternate between the two
+// TMEM accumulators; when a chunk is done the epilogue adds it, round to nearest, into this CTA's fp32 running
+// sum in p.promote_ws (L2-resident, each lane reading back only what it wrote), while the MMAs fill the other
+// accumulator; the last chunk is added to the running sum in the final epilogue.  The truncation then spans
+// one chunk, and the drift falls to roughly 6.4e-9 x sqrt(K x 32 promote_kb).
 #pragma once
 
 #include "gemm_tc2.cuh"
@@ -103,6 +110,24 @@ __device__ __forceinline__ void store_split4(uint32_t hi_addr, uint32_t lo_addr,
                __float_as_uint(__uint_as_float(x1) - __uint_as_float(h1)),
                __float_as_uint(__uint_as_float(x2) - __uint_as_float(h2)),
                __float_as_uint(__uint_as_float(x3) - __uint_as_float(h3)));
+}
+
+// The running sum's 32 values of this lane's row for one 32-column piece: src[j4 * 32], j4 = 0..7 (float4 each;
+// the partial-slot layout).
+__device__ __forceinline__ void load_running_sum(float4 (&s)[8], const float4 *src) {
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) s[j4] = __ldcg(src + j4 * 32);
+}
+
+// v[0..31] (fp32 bits of 32 accumulator columns) += s, rounding to nearest.
+__device__ __forceinline__ void add_running_sum(uint32_t (&v)[32], const float4 (&s)[8]) {
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    v[j4 * 4 + 0] = __float_as_uint(s[j4].x + __uint_as_float(v[j4 * 4 + 0]));
+    v[j4 * 4 + 1] = __float_as_uint(s[j4].y + __uint_as_float(v[j4 * 4 + 1]));
+    v[j4 * 4 + 2] = __float_as_uint(s[j4].z + __uint_as_float(v[j4 * 4 + 2]));
+    v[j4 * 4 + 3] = __float_as_uint(s[j4].w + __uint_as_float(v[j4 * 4 + 3]));
+  }
 }
 
 template <class Cfg>
@@ -319,45 +344,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       SkUnit un;
     int umb, unb;  // the unit's tile (this kernel reads it through tile_coords)
       for (int u = 0; ok && sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
-        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
-          fail(kErrMmaWait);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
-        for (int i = 0; i < un.kb1 - un.kb0; ++i) {
-          if (!mbar_wait_cluster(&ready[sslot], sphase, p.timeout_ns, abort_flag)) {
+        const int steps = un.kb1 - un.kb0;
+        const int G = (p.promote_kb > 0 && p.promote_ws != nullptr) ? p.promote_kb : (steps > 0 ? steps : 1);
+        // chunk [c0, c1) of the unit's k steps, into accumulator `acc` (the epilogue counts the same chunks)
+        for (int c0 = 0; ok && (c0 < steps || c0 == 0); c0 += G) {
+          const int c1 = min(c0 + G, steps);
+          if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
             fail(kErrMmaWait);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_hi = smem_u32(sSplit + sslot * Cfg::SPLIT_BYTES), a_lo = a_hi + Cfg::A_BYTES;
-          const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
+          for (int i = c0; i < c1; ++i) {
+            if (!mbar_wait_cluster(&ready[sslot], sphase, p.timeout_ns, abort_flag)) {
+              fail(kErrMmaWait);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_hi = smem_u32(sSplit + sslot * Cfg::SPLIT_BYTES), a_lo = a_hi + Cfg::A_BYTES;
+            const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-            // A and B^T: K-major 128-byte swizzled rows; k advances 32 bytes inside the row.
-            const uint64_t ah = smem_desc(a_hi + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t al = smem_desc(a_lo + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bh = smem_desc(b_hi + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bl = smem_desc(b_lo + k * 32, 16, 1024, kSwizzle128B);
-            // small terms first
-            tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, (i | k) != 0 ? 1u : 0u);
-            tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
-            tc_mma_tf32_pair(d_tmem, ah, bh, Cfg::IDESC, 1u);
+            for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+              // A and B^T: K-major 128-byte swizzled rows; k advances 32 bytes inside the row.
+              const uint64_t ah = smem_desc(a_hi + k * 32, 16, 1024, kSwizzle128B);
+              const uint64_t al = smem_desc(a_lo + k * 32, 16, 1024, kSwizzle128B);
+              const uint64_t bh = smem_desc(b_hi + k * 32, 16, 1024, kSwizzle128B);
+              const uint64_t bl = smem_desc(b_lo + k * 32, 16, 1024, kSwizzle128B);
+              // small terms first
+              tc_mma_tf32_pair(d_tmem, al, bh, Cfg::IDESC, ((i - c0) | k) != 0 ? 1u : 0u);
+              tc_mma_tf32_pair(d_tmem, ah, bl, Cfg::IDESC, 1u);
+              tc_mma_tf32_pair(d_tmem, ah, bh, Cfg::IDESC, 1u);
+            }
+            tc_commit_pair_mc(&split_empty[sslot], 0x3);
+            if (++sslot == Cfg::SPLIT_STAGES) {
+              sslot = 0;
+              sphase ^= 1u;
+            }
           }
-          tc_commit_pair_mc(&split_empty[sslot], 0x3);
-          if (++sslot == Cfg::SPLIT_STAGES) {
-            sslot = 0;
-            sphase ^= 1u;
+          if (!ok) break;
+          tc_commit_pair_mc(&tfull[acc], 0x3);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
           }
-        }
-        if (!ok) break;
-        tc_commit_pair_mc(&tfull[acc], 0x3);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
         }
       }
       tc_commit_pair(drain);
@@ -383,9 +414,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
       return reinterpret_cast<float4 *>(p.sk_partials + (static_cast<size_t>(w) * 2 + rank) * Cfg::PARTIAL_FLOATS +
                                         static_cast<size_t>(q) * 32 * Cfg::BN);
     };
-    for (int u = 0; sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
+    // This CTA's running sum of a unit's finished chunks (periodic promotion), laid out as the partial slots.
+    float4 *const run = p.promote_ws == nullptr
+                            ? nullptr
+                            : reinterpret_cast<float4 *>(p.promote_ws +
+                                                         (static_cast<size_t>(pair) * 2 + rank) * Cfg::PARTIAL_FLOATS +
+                                                         static_cast<size_t>(q) * 32 * Cfg::BN);
+    bool stop = false;
+    for (int u = 0; !stop && sk_unit(pair, num_pairs, u, p, un, umb, unb); ++u) {
       int mb, nb;
       tile_coords(un.tile, p, mb, nb);
+      const int steps = un.kb1 - un.kb0;
+      const int G = (p.promote_kb > 0 && p.promote_ws != nullptr) ? p.promote_kb : (steps > 0 ? steps : 1);
+      const int chunks = steps > G ? (steps + G - 1) / G : 1;
+      // Every chunk but the last: add it, round to nearest, into the running sum and hand the accumulator back.
+      for (int ch = 0; ch + 1 < chunks; ++ch) {
+        const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
+        if (!__all_sync(0xffffffffu, waited)) {
+          if (lane == 0) fail(kErrEpilogueWait);
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Cfg::BN);
+        const uint32_t tempty_acc = mapa_shared(smem_u32(&tempty[acc]), 0);
+        // 32 columns at a time; the piece's running sum is read from L2 while its TMEM load is in flight.
+#pragma unroll 1
+        for (int c = 0; c < Cfg::BN / 32; ++c) {
+          float4 s_cur[8];
+          if (ch > 0) load_running_sum(s_cur, run + c * 8 * 32 + lane);
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_acc + c * 32, v);
+          tmem_ld_wait();
+          if (c == Cfg::BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_acc);
+          }
+          if (ch > 0) add_running_sum(v, s_cur);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            __stcg(run + (c * 8 + j4) * 32 + lane,
+                   make_float4(__uint_as_float(v[j4 * 4 + 0]), __uint_as_float(v[j4 * 4 + 1]),
+                               __uint_as_float(v[j4 * 4 + 2]), __uint_as_float(v[j4 * 4 + 3])));
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (stop) break;
       const bool waited = mbar_wait(&tfull[acc], acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) fail(kErrEpilogueWait);
@@ -403,6 +481,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c * 32, v);
           tmem_ld_wait();
+          if (chunks > 1) {
+            float4 s4[8];
+            load_running_sum(s4, run + c * 8 * 32 + lane);
+            add_running_sum(v, s4);
+          }
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4)
             __stcg(dst + (c * 8 + j4) * 32 + lane,
@@ -455,6 +538,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c * Cfg::EPI_COLS, v);
           tmem_ld_wait();
+          if (chunks > 1) {
+            float4 s4[8];
+            load_running_sum(s4, run + c * 8 * 32 + lane);
+            add_running_sum(v, s4);
+          }
           if (c == Cfg::BN / Cfg::EPI_COLS - 1) {
             // Last TMEM read of this accumulator: hand it back to the MMA issuer.
             tc_fence_before();

@@ -106,6 +106,21 @@ int tail_split_steps() {
   return steps;
 }
 
+// Periodic promotion of the 3xTF32 kernel (TcParams::promote_kb): k-blocks (32 k each) per chunk of tensor-core
+// accumulation before the epilogue adds the chunk, round to nearest, into an fp32 running sum.  Measured on the
+// reference runner's U(-0.5, 0.5) inputs, 1024^2 x K, max |ref - C| / (1 + |ref|) against fp64 at K = 512 / 1024 /
+// 2048 / 4096: off 1.1e-5 / 6.9e-6 / 2.0e-5 / 5.0e-5; 8 k-blocks 6.2e-6 / 6.9e-6 / 1.2e-5 / 1.3e-5; 4 k-blocks (the
+// default) 3.6e-6 / 4.1e-6 / 6.0e-6 / 8.6e-6 -- inside 1e-5 and below the fp32 fmaf chain's own 1.2e-5 / 1.8e-5
+// at 2048 / 4096.  The running sums cost L2 bandwidth: 2048^3 184 (off) / 159 (8) / 144 (4) TFLOP/s.
+// PF_PROMOTE_KB=<k-blocks> in the environment overrides the default (0 turns it off).
+int promote_kb_default() {
+  static const int kb = [] {
+    const char *e = std::getenv("PF_PROMOTE_KB");
+    return e ? std::max(0, std::atoi(e)) : 4;
+  }();
+  return kb;
+}
+
 template <class... Params, class... Args>
 void launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, int smem, cudaStream_t s, Args &&...args) {
   cudaLaunchConfig_t cfg = {};
@@ -486,6 +501,8 @@ struct pf_ctx {
   int host_chunks = 0;   // pf_set_host_chunks: 0 = default
   unsigned epoch = 0;
   float *sk_ws = nullptr;
+  float *promo_ws = nullptr;  // 3xTF32 periodic promotion: running sums, [pairs][2 CTAs][128 x 256] fp32
+  size_t promo_ws_cap = 0;
   unsigned *sk_flags = nullptr;
   size_t sk_ws_cap = 0, sk_flags_cap = 0;
 
@@ -600,6 +617,25 @@ int encode_maps(pf_ctx *c) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The 3xTF32 kernel's running-sum workspace for `workers` pairs, and the promotion parameters of a launch.
+int set_promotion(pf_ctx *c, int workers, TcParams &p) {
+  if (c->dtype != PF_F32_3XTF32 || promote_kb_default() <= 0) return PF_OK;
+  const size_t ws = static_cast<size_t>(workers) * 2 * 128 * 256 * sizeof(float);
+  if (c->promo_ws_cap < ws) {
+    if (c->promo_ws) cudaFree(c->promo_ws);
+    c->promo_ws = nullptr;
+    c->promo_ws_cap = 0;
+    if (cudaMalloc(&c->promo_ws, ws) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, PF_ENOMEM, "cudaMalloc(%zu) for the 3xTF32 running sums failed", ws);
+    }
+    c->promo_ws_cap = ws;
+  }
+  p.promote_kb = promote_kb_default();
+  p.promote_ws = c->promo_ws;
+  return PF_OK;
+}
 
 // Tiles of the stream-K tail for a CTA-pair launch of `tiles` tiles (0 = pure data-parallel).  With
 // W resident pairs the tail is the partial last wave, R = tiles mod W (all tiles if fewer than W), so a
@@ -716,6 +752,8 @@ int do_launch(pf_ctx *c, cudaStream_t s) {
       p.sk_flags = c->sk_flags;
     }
     dim3 grid(workers * v.cta_per_tile);
+    int prc;
+    if ((prc = set_promotion(c, workers, p))) return prc;
     v.launch_tc(grid, s, c->tmA, c->tmB, c->tmC, c->tmCt, p);
   } else if (v.path == Path::kImage) {
     // The reference's parameter block {&dA,&dB,&dBias,&dC,&M,&N,&K} (cuda_runner.cpp:182).
@@ -806,6 +844,7 @@ int pf_close(pf_ctx *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     cublas_cmp_release(c);
     if (c->sk_ws) cudaFree(c->sk_ws);
+    if (c->promo_ws) cudaFree(c->promo_ws);
     if (c->sk_flags) cudaFree(c->sk_flags);
     if (c->d_status) cudaFree(c->d_status);
     if (c->hbufA) cudaFree(c->hbufA);
@@ -1187,6 +1226,7 @@ int launch_rows(pf_ctx *c, cudaStream_t s, int r0, int rows) {
     p.dir_num_m_blocks = full_m_blocks;
     p.dir_group_m = std::max(1, std::min(c->group_m, full_m_blocks));
     p.dir_workers = sk_tail_tiles(c, full_tiles, p.k_blocks) > 0 ? c->max_units : std::min(full_tiles, c->max_units);
+    if ((rc = set_promotion(c, std::min(p.num_tiles, c->max_units), p))) return rc;
     v.launch_tc(dim3(std::min(p.num_tiles, c->max_units) * v.cta_per_tile), s, tmA, c->tmB, tmC, tmCt, p);
   } else if (v.path == Path::kSimt) {
     dim3 grid((c->N + v.sbn - 1) / v.sbn, (rows + v.sbm - 1) / v.sbm);
