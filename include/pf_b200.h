@@ -50,7 +50,9 @@ typedef enum {
   PF_F32 = 0,          /* fp32 A/B/C, fp32 FFMA (SIMT) accumulate, tanhf epilogue               */
   PF_F32_3XTF32 = 1,   /* fp32 A/B/C; each operand split into tf32 hi + lo, three tf32
                         * tensor-core products per step (lo*hi + hi*lo + hi*hi), fp32 accumulate
-                        * in TMEM, tanhf epilogue: fp32-path tolerance at tensor-core speed      */
+                        * in TMEM in chunks of a few k-blocks, each chunk added round-to-nearest
+                        * into an fp32 running sum (the context's workspace), exp-form GELU:
+                        * fp32-path tolerance at tensor-core speed                              */
   PF_BF16 = 2,         /* bf16 A/B, fp32 accumulate in TMEM, bf16 C                             */
   PF_E4M3 = 3          /* fp8 e4m3 A/B with per-tensor fp32 scales, fp32 accumulate, bf16 C     */
 } pf_dtype;
