@@ -74,6 +74,9 @@ struct Tc2wConfig {
       instr_desc(kDtype == 0 ? 1u : 0u, kDtype == 0 ? 1u : 0u, 0u, 1u, /*M*/ 256, /*N*/ HALF_N);
   static_assert(kEpiWarps == 4 || kEpiWarps == 8, "4 or 8 epilogue warps");
   static_assert(kEpiBufs == 2 || (kEpiBufs == 1 && kEpiWarps == 8), "one staging box only with 8 epilogue warps");
+  // Only the 128-column epilogue (8 warps) takes the staging-box count; the other one (epilogue_rows) alternates
+  // between two boxes per warp, and a single box would let it write into the next warp's box or the barriers.
+  static_assert(EPI_COLS_WARP == 128 || kEpiBufs == 2, "epilogue_rows needs two staging boxes per warp");
   static_assert(SMEM_BYTES <= 232448, "shared memory per block exceeds the sm_100 opt-in limit");
   static_assert(B_CHUNKS_HALF >= 1, "each CTA supplies at least one 128-byte box of B per half");
 };
