@@ -64,9 +64,10 @@ DEFAULT_TILES = {
     "bf16": (256, 256, 32, 8, 16, 1),
     "e4m3": (256, 256, 32, 8, 16, 1),
 }
-# 256 x 512 CTA-pair tiles, 8 epilogue warps (gemm_tc2w.cuh); default_tile picks them for long tiles: 3 stages with
-# two staging boxes per epilogue warp, or, for launches of at most one tile per pair (row shards), 4 stages with one
-# (1,024 x 8192 x 8192: 97.6 -> 96.2 us; 8192^3: 685.0 vs 686.4 us).
+# 256 x 512 CTA-pair tiles, 8 epilogue warps (gemm_tc2w.cuh); default_tile picks them for long tiles: for bf16, 4 stages
+# with one staging box per epilogue warp (bursts of 20, us per launch, 3 -> 4 stages: 8192^3 681.8 -> 678.5, 688.5 ->
+# 684.8, 706.9 -> 703.5 on three boxes; 2,048 x 8192 x 8192 189.2 -> 187.3; 1,024 x 8192 x 8192 96.0 -> 93.5); for
+# e4m3, 3 stages with two staging boxes (16384^3: 2,978 vs 3,032 us), except launches of at most one tile per pair.
 WIDE_TILE = (256, 512, 32, 3, 16, 0)
 WIDE_TILE_DEEP = (256, 512, 32, 4, 16, 0)
 
@@ -86,9 +87,10 @@ def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int
     wave of 74 pairs) ran 6 % faster with 224; 8192-column shards of 1024 / 2048 rows and MLP shards of 4096
     rows ran 1.6-3.7 % slower.
     f32: every SIMT tile gives the same bits (the reference kernel's fmaf chain); small problems get small tiles,
-    larger ones the TMA-fed kernel's 8-row micro-tiles.  Measured TFLOP/s at n^3 (CUDA events, B200): 512: 16.2 on
-    32 x 32 x 32 (TMA-fed 32 x 32: 14.4); 1024: 30.8 on 64 x 32 x 16 (t8x4, TMA) vs 29.1 on 64 x 64 x 16 (t4x4);
-    2048: 44.3 on 64 x 32 x 16 (TMA) vs 38.3 on 128 x 128 x 8 (t8x8); 4096: 47.9 on 128 x 64 x 16 (TMA) vs 45.4.
+    larger ones the TMA-fed kernel's 8-row micro-tiles.  Measured TFLOP/s at n^3 (CUDA events, bursts of 20, B200,
+    packed fp32 FMA): 512: 16.1 on 32 x 32 x 32; 1024: 35.0 on 64 x 32 x 16 (t8x4, TMA); 2048: 48.5 on 64 x 32 x 16
+    (TMA) vs 48.3 on 32 x 64 x 16 (t4x8) and 45.5 on 64 x 64 x 16 (t8x8); 4096: 56.0 on 128 x 64 x 16 (t8x8, TMA)
+    vs 52.5 on 64 x 32 x 16.
     """
     base = DEFAULT_TILES[dtype]
     if dtype == "f32":
@@ -107,7 +109,7 @@ def default_tile(dtype: str, rows: int, N: int, K: int | None = None, pairs: int
         fill512 = t512 / (-(-t512 // pairs) * pairs)
         fill256 = t256 / (-(-t256 // pairs) * pairs)
         if k_steps >= 128 and fill512 >= fill256 - 0.02:
-            return WIDE_TILE_DEEP if t512 <= pairs else WIDE_TILE
+            return WIDE_TILE_DEEP if (dtype == "bf16" or t512 <= pairs) else WIDE_TILE
     t224 = -(-rows // 256) * -(-N // 224)
     tail = t256 % pairs
     if 0 < tail <= pairs // 10 and -(-t224 // pairs) <= -(-t256 // pairs):

@@ -81,13 +81,13 @@ def test_default_tile_choice_follows_the_measurements():
         assert pf.default_tile("bf16", rows, N) == pf.DEFAULT_TILES["bf16"], (rows, N)
     assert pf.default_tile("f32", 2048, 2048) == (64, 32, 16, 8, 4, 0)
     # 256 x 512 tiles for long tiles whose waves are full (1 GPU); the 256-wide kernel elsewhere
-    assert pf.default_tile("bf16", 8192, 8192, 8192) == pf.WIDE_TILE          # 512 tiles, 128 k steps
+    assert pf.default_tile("bf16", 8192, 8192, 8192) == pf.WIDE_TILE_DEEP     # 512 tiles, 128 k steps; bf16: 4 stages
     assert pf.default_tile("e4m3", 16384, 16384, 16384) == pf.WIDE_TILE       # 2048 tiles, 128 k steps
     assert pf.default_tile("bf16", 16384, 14336, 4096) == pf.DEFAULT_TILES["bf16"]   # 64 k steps
     # row shards of 8192^3: 512-wide where both widths fill their waves alike (1,024 and 2,048 rows), 256-wide
     # where 512-wide tiles would fill 86.5 % against 98.8 % (4,096 rows)
     assert pf.default_tile("bf16", 1024, 8192, 8192) == pf.WIDE_TILE_DEEP   # 64 tiles: one per pair, 4 stages
-    assert pf.default_tile("bf16", 2048, 8192, 8192) == pf.WIDE_TILE
+    assert pf.default_tile("bf16", 2048, 8192, 8192) == pf.WIDE_TILE_DEEP
     assert pf.default_tile("bf16", 4096, 8192, 8192) == pf.DEFAULT_TILES["bf16"]
     assert pf.default_tile("e4m3", 2048, 16384, 16384) == pf.DEFAULT_TILES["e4m3"]  # 3.5 vs 6.9 waves
     # fp32 SIMT (same bits on every tile): small tiles for small problems, the TMA-fed kernel's 64 x 32 tiles up to

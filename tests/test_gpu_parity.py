@@ -468,7 +468,7 @@ def test_512_wide_tiles_on_row_shards(ctx, oracle_mod, pf, rows):
     # stream-K is opt-in), and the same shards with row-band stream-K forced on (4 / 8 bands of 18 / 9 pairs)
     w = wl.CONFIGS["cfg3_bf16_8192"]
     ws = wl.scaled(w, rows, w.N, w.K)
-    assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == (pf.WIDE_TILE_DEEP if rows == 1024 else pf.WIDE_TILE)
+    assert pf.default_tile(ws.dtype, rows, ws.N, ws.K) == pf.WIDE_TILE_DEEP
     inp = wl.make_inputs(ws, seed=53)
     A, B, bias, C = device_operands(ws, inp)
     run_pf(ctx, ws, inp, None, (A, B, bias, C))
