@@ -212,8 +212,9 @@ def _stream(s) -> int:
 class Context:
     """One pf_ctx: a GPU, a stream, a prepared kernel variant and bound operands."""
 
-    def __init__(self, device: int = 0):
-        self._lib = load_library()
+    def __init__(self, device: int = 0, lib: ctypes.CDLL | None = None):
+        # `lib`: a library handle from load_library(path) (another build of libpf_b200.so); default the package's.
+        self._lib = lib if lib is not None else load_library()
         h = ctypes.c_void_p()
         rc = self._lib.pf_open(device, ctypes.byref(h))
         if rc:

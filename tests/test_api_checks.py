@@ -61,3 +61,13 @@ def test_noalloc_checks_torch_operands_before_the_c_abi():
         pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 128, 32, 48, A, B, bias, C)
     with pytest.raises(ValueError, match="CUDA tensor on device 0"):
         pf.gemm_bias_gelu_noalloc(0, "bf16", tile, 64, 32, 48, A, B, bias, C)
+
+
+def test_timetiles_cli_refuses_unknown_dtypes_before_touching_a_gpu():
+    """python -m ptxforge_b200.timetiles: argument errors end the run before any operand or context exists."""
+    import pytest
+    from ptxforge_b200 import timetiles
+    with pytest.raises(SystemExit):
+        timetiles.main(["fp64", "16", "16", "16"])
+    with pytest.raises(SystemExit):
+        timetiles.main(["bf16", "16", "16"])
