@@ -5,7 +5,8 @@ inputs, the reference gate's metric core/src/cuda_runner.cpp:196):
     fp32  1e-5        bf16  2e-2        e4m3  5e-2
 plus: the fp32 path is bit-identical to the reference's own kernel (kernels/gemm_bias_gelu.cu built for
 sm_100a, oracle/_ref/), and at the full BASELINE sizes every output is compared with a plain PyTorch
-fp32 computation of the same op (TF32 off) and the reference gate's 512 sampled fp64 points.
+fp32 computation of the same op (TF32 off), 64 whole rows with the oracle's fp64 result, and the reference
+gate's 512 sampled fp64 points.
 """
 import os
 
@@ -189,6 +190,12 @@ def test_full_size_gate_torch_and_determinism(ctx, oracle_mod, name):
     scale = inp.scale_a * inp.scale_b
     err, _, _ = oracle_mod.sampled_gate(inp.A, inp.B, inp.bias, Cn, scale=scale, samples=512, seed=99)
     assert err <= TOL[w.dtype], f"sampled gate {err:.3e}"
+    # whole rows against the oracle's fp64 result: 64 rows spread over every 128-row block of the launch (every
+    # column tile, both CTAs of a pair, first and last row), not just the gate's 512 points
+    rows = np.unique(np.concatenate([np.linspace(0, w.M - 1, 62).astype(np.int64), [1, w.M - 2]]))
+    ref_rows = oracle_mod.full_f64(inp.A[rows], inp.B, inp.bias, scale)
+    e_rows = oracle_mod.max_rel_err(ref_rows, Cn[rows])
+    assert e_rows <= TOL[w.dtype], f"{len(rows)} whole rows vs the fp64 oracle: {e_rows:.3e}"
     ref = torch_fp32_reference(A, B, bias, scale)
     e2 = max_rel_err_t(ref, C)
     del ref
